@@ -1,0 +1,975 @@
+// paged_attention.cu -- split-KV decode / block-verify attention over the paged
+// BF16-K / (BF16 | E4M3)-V pool, and over contiguous (B, KV, T, D) tensors.
+//
+// What it computes (the eager branch of SelfAttention.forward,
+// specdec/engine/model_self.py:740-775, and reference.attention,
+// specdec/kernels/reference.py:47-56):
+//     out[b, h, i] = softmax_j( q[b,h,i] . k[b,h/n_rep,j] * sm_scale ) . v[b,h/n_rep,j]
+// over keys j <= i + (T - S) (reference.py:40-44; S == 1 sees every key), with
+// GQA handled by sharing one K/V stream among the n_rep query heads of a KV
+// head instead of materialising kv_repeat (model_self.py:294-298).  For an E4M3
+// V cache the dequantisation of model_self.py:316-320 happens inside the PV
+// product: the per-token scale is folded into the probabilities and the codes
+// feed the tensor cores as exact f16 values.
+//
+// Launch structure (one attention call):
+//   1. plan_kernel     (1 CTA)   device lengths -> work items (seq, kv head,
+//                                query tile, key-block range) + merge groups.
+//                                One plan serves all layers of a step.
+//   2. split_kernel    (1 CTA per work item) warp 4 streams the item's pages
+//                                with bulk TMA into an 8-deep mbarrier ring;
+//                                warps 0-3 run QK^T and PV on the tensor cores
+//                                (m16n8k16, fp32 accumulate) with an online
+//                                softmax, then merge their key slices in smem.
+//   3. merge_kernel    (1 CTA per (group, row)) log-sum-exp merge of the
+//                                split partials of groups with >1 split.
+#include <cudaTypedefs.h>
+
+#include <math.h>
+
+#include "sd_common.cuh"
+#include "sd_internal.h"
+
+namespace sd {
+
+// ---------------------------------------------------------------- plan records
+struct WorkItem {             // 32 bytes
+  int32_t b, h, q0, nq;       // sequence, kv head, first query row, query rows in the tile
+  int32_t page_begin, page_end;  // key blocks [page_begin, page_end) of 16 tokens
+  int32_t group, nsplit;      // merge group; splits in the group (1 = write the output directly)
+};
+struct GroupInfo {
+  int32_t first_item, nsplit, b, h, q0, nq, pad0, pad1;
+};
+struct PlanHeader {
+  int32_t num_items, pages_per_split, num_groups, total_pages;
+  int32_t pad[60];
+};
+static_assert(sizeof(PlanHeader) == 256, "plan header is 256 bytes");
+
+constexpr int kMaxRows = 64;  // query rows (n_rep x query positions) per work item
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kStages = 8;
+
+struct WsLayout {
+  size_t items, groups, lse, po, total;
+  int32_t max_items, max_groups;
+};
+
+static WsLayout ws_layout(int B, int KV, int max_qtiles, int D, int target_items) {
+  WsLayout w;
+  w.max_groups = B * max_qtiles * KV;
+  w.max_items = target_items + w.max_groups;
+  w.items = sizeof(PlanHeader);
+  w.groups = align_up(w.items + sizeof(WorkItem) * (size_t)w.max_items, 256);
+  w.lse = align_up(w.groups + sizeof(GroupInfo) * (size_t)w.max_groups, 256);
+  w.po = align_up(w.lse + sizeof(float) * kMaxRows * (size_t)w.max_items, 256);
+  w.total = align_up(w.po + sizeof(float) * kMaxRows * (size_t)D * w.max_items, 256);
+  return w;
+}
+
+struct AttnParams {
+  const __nv_bfloat16* q;
+  __nv_bfloat16* out;
+  int64_t q_st, q_sh, o_st, o_sh;
+  const int32_t* q_row0;
+  const int32_t* q_len;
+  const int32_t* ctx_len;
+  int32_t uni_q_len, uni_ctx_len, uni_row_stride;  // used where the arrays are NULL
+  int32_t B, H, KV, n_rep, max_q_len, q_tile, max_qtiles;
+  const uint8_t* k_pool;
+  const uint8_t* v_pool;
+  const float* v_scale;
+  const int32_t* page_table;
+  int32_t num_pages, max_pages;
+  float scale_log2;
+  PlanHeader* hdr;
+  WorkItem* items;
+  GroupInfo* groups;
+  float* p_lse;
+  float* p_o;
+  int32_t max_items, max_groups, target_items;
+  int32_t* status;
+};
+
+SD_DEV int seq_q_len(const AttnParams& p, int b) { return p.q_len ? p.q_len[b] : p.uni_q_len; }
+SD_DEV int seq_ctx_len(const AttnParams& p, int b) { return p.ctx_len ? p.ctx_len[b] : p.uni_ctx_len; }
+SD_DEV int seq_row0(const AttnParams& p, int b) { return p.q_row0 ? p.q_row0[b] : b * p.uni_row_stride; }
+
+// ---------------------------------------------------------------- plan
+// Key blocks a (sequence, query tile) group must read, or 0 for an empty /
+// invalid group.  Invalid lengths are reported once per sequence.
+SD_DEV int group_pages(const AttnParams& p, int gi, int& b, int& h, int& q0, int& nq) {
+  const int per_b = p.max_qtiles * p.KV;
+  b = gi / per_b;
+  const int rem = gi - b * per_b;
+  const int qt = rem / p.KV;
+  h = rem - qt * p.KV;
+  const int qlen = seq_q_len(p, b);
+  const int ctx = seq_ctx_len(p, b);
+  q0 = qt * p.q_tile;
+  nq = min(p.q_tile, qlen - q0);
+  if (qlen <= 0 || nq <= 0) return 0;
+  if (qlen > p.max_q_len || ctx < qlen) {
+    if (qt == 0 && h == 0) raise_status(p.status, SPECDEC_STATUS_BAD_LENGTH);
+    return 0;
+  }
+  if (ctx > p.max_pages * kPage) {
+    if (qt == 0 && h == 0) raise_status(p.status, SPECDEC_STATUS_PAGE_OVERFLOW);
+    return 0;
+  }
+  const int visible = q0 + nq + (ctx - qlen);  // keys seen by the last row of the tile
+  return (visible + kPage - 1) / kPage;
+}
+
+// Exclusive block scan of one int per thread (blockDim.x <= 1024); returns the
+// block total through `total`.
+SD_DEV int block_exclusive_scan(int v, int& total, int* s_warp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = (blockDim.x + 31) >> 5;
+    int w = lane < nw ? s_warp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    s_warp[lane] = w;  // inclusive prefix of warp totals
+  }
+  __syncthreads();
+  const int before = warp > 0 ? s_warp[warp - 1] : 0;
+  total = s_warp[((blockDim.x + 31) >> 5) - 1];
+  __syncthreads();
+  return before + x - v;
+}
+
+__global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
+  __shared__ int s_warp[32];
+  __shared__ long long s_total;
+  const int ngroups = p.max_groups;
+  if (threadIdx.x == 0) s_total = 0;
+  __syncthreads();
+  long long local = 0;
+  for (int gi = threadIdx.x; gi < ngroups; gi += blockDim.x) {
+    int b, h, q0, nq;
+    local += group_pages(p, gi, b, h, q0, nq);
+  }
+  // warp reduce then one atomic per warp
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
+  if ((threadIdx.x & 31) == 0) atomicAdd(reinterpret_cast<unsigned long long*>(&s_total),
+                                         static_cast<unsigned long long>(local));
+  __syncthreads();
+  const long long total = s_total;
+  int pps = static_cast<int>((total + p.target_items - 1) / p.target_items);
+  pps = max(pps, 1);
+
+  int carry = 0;
+  for (int base = 0; base < ngroups; base += blockDim.x) {
+    const int gi = base + threadIdx.x;
+    int b = 0, h = 0, q0 = 0, nq = 0, pages = 0;
+    if (gi < ngroups) pages = group_pages(p, gi, b, h, q0, nq);
+    const int n = (pages + pps - 1) / pps;
+    int chunk_total;
+    const int first = carry + block_exclusive_scan(n, chunk_total, s_warp);
+    if (gi < ngroups) {
+      GroupInfo g;
+      g.first_item = first;
+      g.nsplit = n;
+      g.b = b;
+      g.h = h;
+      g.q0 = q0;
+      g.nq = nq;
+      g.pad0 = g.pad1 = 0;
+      p.groups[gi] = g;
+      for (int s = 0; s < n; ++s) {
+        WorkItem it;
+        it.b = b;
+        it.h = h;
+        it.q0 = q0;
+        it.nq = nq;
+        it.page_begin = s * pps;
+        it.page_end = min((s + 1) * pps, pages);
+        it.group = gi;
+        it.nsplit = n;
+        p.items[first + s] = it;
+      }
+    }
+    carry += chunk_total;
+  }
+  if (threadIdx.x == 0) {
+    p.hdr->num_items = carry;
+    p.hdr->pages_per_split = pps;
+    p.hdr->num_groups = ngroups;
+    p.hdr->total_pages = static_cast<int32_t>(total);
+  }
+}
+
+// ---------------------------------------------------------------- split kernel
+template <int D, bool VF8>
+struct StageGeom {
+  static constexpr int KB = D * 32;                 // 16 tokens x D x bf16
+  static constexpr int VB = VF8 ? D * 16 : D * 32;  // E4M3 codes or bf16
+  static constexpr int SB = VF8 ? 64 : 0;           // 16 fp32 scales
+  static constexpr int BYTES = ((KB + VB + SB + 1023) / 1024) * 1024;
+  static constexpr int SMEM = kStages * BYTES + 1024;  // + alignment slack
+  static constexpr int MERGE_ROW = D + 8;              // padded fp32 row in the merge area
+  static constexpr int MERGE_WARP = 16 * MERGE_ROW * 4 + 256;
+  static_assert(kConsumerWarps * MERGE_WARP <= kStages * BYTES, "merge area fits in the ring");
+};
+
+template <int D, bool VF8, bool TMAP>
+__global__ void __launch_bounds__(kThreads) split_kernel(const AttnParams p,
+                                                         const __grid_constant__ CUtensorMap kmap,
+                                                         const __grid_constant__ CUtensorMap vmap) {
+  using Geo = StageGeom<D, VF8>;
+  constexpr int NKK = D / 16;  // k-steps of QK^T
+  constexpr int NNT = D / 8;   // n-tiles of PV
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t full_bar[kStages];
+  __shared__ uint64_t empty_bar[kStages];
+  __shared__ int s_abort;
+  __shared__ int s_issued;
+
+  if (static_cast<int>(blockIdx.x) >= p.hdr->num_items) return;  // uniform per CTA
+  const WorkItem it = p.items[blockIdx.x];
+  const int R = p.n_rep * it.nq;
+  int G = (R + 15) >> 4;
+  if (G == 3) G = 4;
+  const int KS = kConsumerWarps / G;
+  const int npages = it.page_end - it.page_begin;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], G);
+    }
+    s_abort = 0;
+    s_issued = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  // per-thread softmax state (consumers)
+  float o[NNT][4];
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f, sref = 0.f;
+  const int gq = lane >> 2, cq = lane & 3;
+  const int g = warp % G;
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------------------------ producer: one elected lane
+    if (lane == 0) {
+      if (TMAP) {
+        prefetch_tmap(&kmap);
+        prefetch_tmap(&vmap);
+      }
+      int li = 0;
+      for (; li < npages; ++li) {
+        const int slot = li % kStages;
+        if (li >= kStages) {
+          if (!mbar_wait(&empty_bar[slot], ((li / kStages) - 1) & 1)) {
+            raise_status(p.status, SPECDEC_STATUS_TIMEOUT);
+            atomicExch(&s_abort, 1);
+            break;
+          }
+        }
+        if (*reinterpret_cast<volatile int*>(&s_abort)) break;
+        uint8_t* st = smem + slot * Geo::BYTES;
+        const int blk = it.page_begin + li;
+        if (TMAP) {
+          mbar_arrive_expect_tx(&full_bar[slot], Geo::KB + Geo::VB);
+          const int plane = it.b * p.KV + it.h;
+#pragma unroll
+          for (int hf = 0; hf < D / 64; ++hf) {
+            tma_load_3d(st + hf * 2048, &kmap, hf * 64, blk * kPage, plane, &full_bar[slot]);
+            tma_load_3d(st + Geo::KB + hf * 2048, &vmap, hf * 64, blk * kPage, plane, &full_bar[slot]);
+          }
+        } else {
+          const int page = __ldg(p.page_table + static_cast<int64_t>(it.b) * p.max_pages + blk);
+          if (page < 0 || page >= p.num_pages) {
+            raise_status(p.status, SPECDEC_STATUS_BAD_PAGE);
+            mbar_arrive(&full_bar[slot]);  // complete the phase without data
+            continue;
+          }
+          const int64_t ph = static_cast<int64_t>(page) * p.KV + it.h;
+          mbar_arrive_expect_tx(&full_bar[slot], Geo::KB + Geo::VB + Geo::SB);
+          bulk_g2s(st, p.k_pool + ph * Geo::KB, Geo::KB, &full_bar[slot]);
+          bulk_g2s(st + Geo::KB, p.v_pool + ph * Geo::VB, Geo::VB, &full_bar[slot]);
+          if (VF8) bulk_g2s(st + Geo::KB + Geo::VB, p.v_scale + ph * kPage, Geo::SB, &full_bar[slot]);
+        }
+      }
+      s_issued = li;
+    }
+  } else {
+    // ------------------------------------------------ consumers
+    const int ks = warp / G;
+    const int qlen = seq_q_len(p, it.b);
+    const int ctx = seq_ctx_len(p, it.b);
+    const int row0 = seq_row0(p, it.b);
+    const int ra = g * 16 + gq, rb = ra + 8;
+    int lim_a = -1, lim_b = -1;
+    uint32_t qf[NKK][4];
+    {
+      const __nv_bfloat16* qa = nullptr;
+      const __nv_bfloat16* qb = nullptr;
+      if (ra < R) {
+        const int hh = ra / it.nq, qi = it.q0 + ra % it.nq;
+        qa = p.q + static_cast<int64_t>(row0 + qi) * p.q_st + static_cast<int64_t>(it.h * p.n_rep + hh) * p.q_sh;
+        lim_a = qi + ctx - qlen;
+      }
+      if (rb < R) {
+        const int hh = rb / it.nq, qi = it.q0 + rb % it.nq;
+        qb = p.q + static_cast<int64_t>(row0 + qi) * p.q_st + static_cast<int64_t>(it.h * p.n_rep + hh) * p.q_sh;
+        lim_b = qi + ctx - qlen;
+      }
+#pragma unroll
+      for (int kk = 0; kk < NKK; ++kk) {
+        const int d0 = kk * 16 + 2 * cq;
+        qf[kk][0] = qa ? *reinterpret_cast<const uint32_t*>(qa + d0) : 0u;
+        qf[kk][1] = qb ? *reinterpret_cast<const uint32_t*>(qb + d0) : 0u;
+        qf[kk][2] = qa ? *reinterpret_cast<const uint32_t*>(qa + d0 + 8) : 0u;
+        qf[kk][3] = qb ? *reinterpret_cast<const uint32_t*>(qb + d0 + 8) : 0u;
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NNT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+
+    for (int li = ks; li < npages; li += KS) {
+      const int slot = li % kStages;
+      // every lane polls; the give-up decision is made warp-wide so the warp
+      // leaves the loop together (the shuffles below need all 32 lanes)
+      if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[slot], (li / kStages) & 1))) {
+        raise_status(p.status, SPECDEC_STATUS_TIMEOUT);
+        atomicExch(&s_abort, 1);
+        break;
+      }
+      const uint32_t kb = smem_u32(smem + slot * Geo::BYTES);
+      const uint32_t vb = kb + Geo::KB;
+
+      // S = Q K^T for this block's 16 keys: tile 0 = keys 0-7, tile 1 = keys 8-15
+      float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+      {
+        const int key = (lane & 7) + ((lane >> 4) << 3);
+        const int csel = (lane >> 3) & 1;
+#pragma unroll
+        for (int kk = 0; kk < NKK; ++kk) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(kb + kblock_chunk_offset(key, 2 * kk + csel), b0, b1, b2, b3);
+          mma_bf16(s0, qf[kk], b0, b1);
+          mma_bf16(s1, qf[kk], b2, b3);
+        }
+      }
+      const int key0 = (it.page_begin + li) * kPage;
+      const int ka = key0 + 2 * cq;
+      float xa[4] = {s0[0], s0[1], s1[0], s1[1]};
+      float xb[4] = {s0[2], s0[3], s1[2], s1[3]};
+      const int kx[4] = {ka, ka + 1, ka + 8, ka + 9};
+      float mxa = -INFINITY, mxb = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        xa[e] = (kx[e] <= lim_a) ? xa[e] * p.scale_log2 : -INFINITY;
+        xb[e] = (kx[e] <= lim_b) ? xb[e] * p.scale_log2 : -INFINITY;
+        mxa = fmaxf(mxa, xa[e]);
+        mxb = fmaxf(mxb, xb[e]);
+      }
+      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));
+      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 2));
+      mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
+      mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
+      const float mna = fmaxf(m_a, mxa), mnb = fmaxf(m_b, mxb);
+      const float ua = (mna == -INFINITY) ? 0.f : mna;
+      const float ub = (mnb == -INFINITY) ? 0.f : mnb;
+      float alpha_a = fast_exp2(m_a - ua), alpha_b = fast_exp2(m_b - ub);
+      m_a = mna;
+      m_b = mnb;
+      float pa[4], pb[4];
+      float suma = 0.f, sumb = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        pa[e] = fast_exp2(xa[e] - ua);
+        pb[e] = fast_exp2(xb[e] - ub);
+        suma += pa[e];
+        sumb += pb[e];
+      }
+      l_a = l_a * alpha_a + suma;
+      l_b = l_b * alpha_b + sumb;
+
+      uint32_t pf[4];
+      if (VF8) {
+        // fold the per-token V scales into P; keep the accumulator in units of
+        // the running maximum scale `sref` so P * s / sref stays in [0, 1].
+        const float* sc = reinterpret_cast<const float*>(smem + slot * Geo::BYTES + Geo::KB + Geo::VB);
+        float sl = (key0 + (lane & 15) < ctx) ? sc[lane & 15] : 0.f;
+        sl = fmaxf(sl, __shfl_xor_sync(0xffffffffu, sl, 8));
+        sl = fmaxf(sl, __shfl_xor_sync(0xffffffffu, sl, 4));
+        sl = fmaxf(sl, __shfl_xor_sync(0xffffffffu, sl, 2));
+        sl = fmaxf(sl, __shfl_xor_sync(0xffffffffu, sl, 1));
+        const float nref = fmaxf(sref, sl);
+        if (nref > sref) {
+          const float ratio = sref / nref;  // 0 on the first block: o is still zero
+          alpha_a *= ratio;
+          alpha_b *= ratio;
+          sref = nref;
+        }
+        const float inv = (sref > 0.f) ? 1.f / sref : 0.f;
+        const float2 s01 = *reinterpret_cast<const float2*>(sc + 2 * cq);
+        const float2 s89 = *reinterpret_cast<const float2*>(sc + 8 + 2 * cq);
+        const float sk[4] = {s01.x * inv, s01.y * inv, s89.x * inv, s89.y * inv};
+        pf[0] = pack_f16(pa[0] * sk[0], pa[1] * sk[1]);
+        pf[1] = pack_f16(pb[0] * sk[0], pb[1] * sk[1]);
+        pf[2] = pack_f16(pa[2] * sk[2], pa[3] * sk[3]);
+        pf[3] = pack_f16(pb[2] * sk[2], pb[3] * sk[3]);
+      } else {
+        pf[0] = pack_bf16(pa[0], pa[1]);
+        pf[1] = pack_bf16(pb[0], pb[1]);
+        pf[2] = pack_bf16(pa[2], pa[3]);
+        pf[3] = pack_bf16(pb[2], pb[3]);
+      }
+      if (__any_sync(0xffffffffu, alpha_a != 1.f || alpha_b != 1.f)) {
+#pragma unroll
+        for (int nt = 0; nt < NNT; ++nt) {
+          o[nt][0] *= alpha_a;
+          o[nt][1] *= alpha_a;
+          o[nt][2] *= alpha_b;
+          o[nt][3] *= alpha_b;
+        }
+      }
+      // O += P V
+      if (VF8) {
+        const uint8_t* vrow = smem + slot * Geo::BYTES + Geo::KB;
+#pragma unroll
+        for (int nt = 0; nt < NNT; ++nt) {
+          const uint32_t w = *reinterpret_cast<const uint32_t*>(vrow + (nt * 8 + gq) * 16 + 4 * cq);
+          mma_f16(o[nt], pf, e4m3x2_to_f16x2(w), e4m3x2_to_f16x2(w >> 16));
+        }
+      } else {
+        const int key = (lane & 7) + (((lane >> 3) & 1) << 3);
+        const int csel = lane >> 4;
+#pragma unroll
+        for (int nt = 0; nt < NNT; nt += 2) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_trans(vb + kblock_chunk_offset(key, nt + csel), b0, b1, b2, b3);
+          mma_bf16(o[nt], pf, b0, b1);
+          mma_bf16(o[nt + 1], pf, b2, b3);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[slot]);
+    }
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+  }
+  __syncthreads();  // (A) every page consumed, every copy landed; the ring is free
+
+  const bool aborted = *reinterpret_cast<volatile int*>(&s_abort) != 0;
+  if (!aborted && warp < kConsumerWarps) {
+    uint8_t* area = smem + warp * Geo::MERGE_WARP;
+    float* om = reinterpret_cast<float*>(area);
+    float* mm = reinterpret_cast<float*>(area + 16 * Geo::MERGE_ROW * 4);
+    float* lm = mm + 16;
+    const float f = VF8 ? sref : 1.f;
+#pragma unroll
+    for (int nt = 0; nt < NNT; ++nt) {
+      const int d = nt * 8 + 2 * cq;
+      *reinterpret_cast<float2*>(om + gq * Geo::MERGE_ROW + d) = make_float2(o[nt][0] * f, o[nt][1] * f);
+      *reinterpret_cast<float2*>(om + (gq + 8) * Geo::MERGE_ROW + d) = make_float2(o[nt][2] * f, o[nt][3] * f);
+    }
+    if (cq == 0) {
+      mm[gq] = m_a;
+      mm[gq + 8] = m_b;
+      lm[gq] = l_a;
+      lm[gq + 8] = l_b;
+    }
+  }
+  __syncthreads();  // (B)
+
+  if (!aborted && threadIdx.x < kConsumerWarps * 32) {
+    const int qlen = seq_q_len(p, it.b);
+    (void)qlen;
+    const int row0 = seq_row0(p, it.b);
+    const int units = R * (D / 4);
+    for (int u = threadIdx.x; u < units; u += kConsumerWarps * 32) {
+      const int r = u / (D / 4);
+      const int d = (u - r * (D / 4)) * 4;
+      const int rg = r >> 4, rr = r & 15;
+      float M = -INFINITY;
+      for (int ks = 0; ks < KS; ++ks) {
+        const float* mm = reinterpret_cast<const float*>(smem + (rg + G * ks) * Geo::MERGE_WARP +
+                                                         16 * Geo::MERGE_ROW * 4);
+        M = fmaxf(M, mm[rr]);
+      }
+      float L = 0.f;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (M != -INFINITY) {
+        for (int ks = 0; ks < KS; ++ks) {
+          const uint8_t* area = smem + (rg + G * ks) * Geo::MERGE_WARP;
+          const float* mm = reinterpret_cast<const float*>(area + 16 * Geo::MERGE_ROW * 4);
+          const float w = fast_exp2(mm[rr] - M);
+          L += mm[16 + rr] * w;
+          const float4 v = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(area) +
+                                                            rr * Geo::MERGE_ROW + d);
+          acc.x += v.x * w;
+          acc.y += v.y * w;
+          acc.z += v.z * w;
+          acc.w += v.w * w;
+        }
+      }
+      const float inv = (L > 0.f) ? 1.f / L : 0.f;
+      acc.x *= inv;
+      acc.y *= inv;
+      acc.z *= inv;
+      acc.w *= inv;
+      if (it.nsplit == 1) {
+        const int hh = r / it.nq, qi = it.q0 + r % it.nq;
+        __nv_bfloat16* dst = p.out + static_cast<int64_t>(row0 + qi) * p.o_st +
+                             static_cast<int64_t>(it.h * p.n_rep + hh) * p.o_sh + d;
+        uint2 pk;
+        pk.x = pack_bf16(acc.x, acc.y);
+        pk.y = pack_bf16(acc.z, acc.w);
+        *reinterpret_cast<uint2*>(dst) = pk;
+      } else {
+        float* po = p.p_o + (static_cast<int64_t>(blockIdx.x) * kMaxRows + r) * D + d;
+        *reinterpret_cast<float4*>(po) = acc;
+        if (d == 0) p.p_lse[static_cast<int64_t>(blockIdx.x) * kMaxRows + r] = (L > 0.f) ? M + fast_log2(L) : -INFINITY;
+      }
+    }
+  }
+
+  if (aborted && threadIdx.x == 0) {
+    // let the copies this CTA issued land before it retires (bounded)
+    const int issued = *reinterpret_cast<volatile int*>(&s_issued);
+    for (int li = max(0, issued - kStages); li < issued; ++li) {
+      (void)mbar_wait(&full_bar[li % kStages], (li / kStages) & 1);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- merge kernel
+// One CTA per (group, query row); 128 threads = 4 split lanes x 32 dim quads.
+template <int D>
+__global__ void __launch_bounds__(128) merge_kernel(const AttnParams p) {
+  const int gi = blockIdx.x;
+  if (gi >= p.hdr->num_groups) return;
+  const GroupInfo grp = p.groups[gi];
+  if (grp.nsplit <= 1) return;
+  const int R = p.n_rep * grp.nq;
+  const int r = blockIdx.y;
+  if (r >= R) return;
+  constexpr int NQ = D / 4;
+  constexpr int NL = 128 / NQ;  // split lanes
+  const int dq = threadIdx.x % NQ, sl = threadIdx.x / NQ;
+  __shared__ float s_w[256];
+  __shared__ float s_M;
+  __shared__ float4 s_acc[NL][NQ];
+  __shared__ float s_L[NL];
+  if (threadIdx.x == 0) {
+    float M = -INFINITY;
+    for (int s = 0; s < grp.nsplit; ++s)
+      M = fmaxf(M, p.p_lse[static_cast<int64_t>(grp.first_item + s) * kMaxRows + r]);
+    s_M = M;
+  }
+  __syncthreads();
+  const float M = s_M;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float L = 0.f;
+  if (M != -INFINITY) {
+    for (int s = sl; s < grp.nsplit; s += NL) {
+      const int64_t idx = static_cast<int64_t>(grp.first_item + s) * kMaxRows + r;
+      const float w = fast_exp2(p.p_lse[idx] - M);
+      const float4 v = *reinterpret_cast<const float4*>(p.p_o + idx * D + dq * 4);
+      acc.x += v.x * w;
+      acc.y += v.y * w;
+      acc.z += v.z * w;
+      acc.w += v.w * w;
+      L += w;
+    }
+  }
+  (void)s_w;
+  s_acc[sl][dq] = acc;
+  if (dq == 0) s_L[sl] = L;
+  __syncthreads();
+  if (sl == 0) {
+    float4 a = s_acc[0][dq];
+    float Lt = s_L[0];
+    for (int k = 1; k < NL; ++k) {
+      const float4 b = s_acc[k][dq];
+      a.x += b.x;
+      a.y += b.y;
+      a.z += b.z;
+      a.w += b.w;
+      Lt += s_L[k];
+    }
+    const float inv = Lt > 0.f ? 1.f / Lt : 0.f;
+    const int hh = r / grp.nq, qi = grp.q0 + r % grp.nq;
+    const int row0 = seq_row0(p, grp.b);
+    __nv_bfloat16* dst = p.out + static_cast<int64_t>(row0 + qi) * p.o_st +
+                         static_cast<int64_t>(grp.h * p.n_rep + hh) * p.o_sh + dq * 4;
+    uint2 pk;
+    pk.x = pack_bf16(a.x * inv, a.y * inv);
+    pk.y = pack_bf16(a.z * inv, a.w * inv);
+    *reinterpret_cast<uint2*>(dst) = pk;
+  }
+}
+
+// ---------------------------------------------------------------- fp32 contiguous path
+// CUDA-core kernel for the f32 dtype of the reference op (attention.cu:262-272).
+// One CTA per (b, h, query row); keys in chunks of 128: warps compute the
+// chunk's scores into shared memory, then threads over `d` accumulate P.V.
+__global__ void __launch_bounds__(128) attn_f32_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                                                       const float* __restrict__ v, float* __restrict__ out,
+                                                       int H, int KV, int S, int T, int D, float sm_scale) {
+  const int i = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (H / KV);
+  __shared__ float s_q[128];
+  __shared__ float s_p[128];
+  __shared__ float s_red[4];
+  __shared__ float s_stat[2];
+  const float* qrow = q + ((static_cast<int64_t>(b) * H + h) * S + i) * D;
+  const float* kb = k + (static_cast<int64_t>(b) * KV + kvh) * T * D;
+  const float* vb = v + (static_cast<int64_t>(b) * KV + kvh) * T * D;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) s_q[d] = qrow[d];
+  __syncthreads();
+  const int nvis = min(T, i + (T - S) + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float m_run = -INFINITY, l_run = 0.f, acc = 0.f;
+  for (int j0 = 0; j0 < nvis; j0 += 128) {
+    const int nc = min(128, nvis - j0);
+    for (int jj = warp; jj < nc; jj += 4) {
+      const float* kr = kb + static_cast<int64_t>(j0 + jj) * D;
+      float part = 0.f;
+      for (int d = lane; d < D; d += 32) part += s_q[d] * kr[d];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+      if (lane == 0) s_p[jj] = part * sm_scale;
+    }
+    __syncthreads();
+    float mx = (threadIdx.x < nc) ? s_p[threadIdx.x] : -INFINITY;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) s_red[warp] = mx;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const float cm = fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3]));
+      s_stat[0] = fmaxf(m_run, cm);
+    }
+    __syncthreads();
+    const float m_new = s_stat[0];
+    float e = 0.f;
+    if (threadIdx.x < nc) {
+      e = expf(s_p[threadIdx.x] - m_new);
+      s_p[threadIdx.x] = e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) e += __shfl_xor_sync(0xffffffffu, e, o);
+    __syncthreads();
+    if (lane == 0) s_red[warp] = e;
+    __syncthreads();
+    const float csum = s_red[0] + s_red[1] + s_red[2] + s_red[3];
+    const float alpha = expf(m_run - m_new);
+    l_run = l_run * alpha + csum;
+    if (threadIdx.x < D) {
+      float a = acc * alpha;
+      for (int jj = 0; jj < nc; ++jj) a += s_p[jj] * vb[static_cast<int64_t>(j0 + jj) * D + threadIdx.x];
+      acc = a;
+    }
+    m_run = m_new;
+    __syncthreads();
+  }
+  if (threadIdx.x < D) {
+    out[((static_cast<int64_t>(b) * H + h) * S + i) * D + threadIdx.x] = (l_run > 0.f) ? acc / l_run : 0.f;
+  }
+}
+
+// ---------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult qres;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &qres) == cudaSuccess &&
+        qres == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 3-D map over a contiguous (B*KV, T, D) bf16 tensor with a {64, 16, 1} box and
+// 128-byte swizzle; out-of-range rows read as zero.
+static int encode_kv_map(CUtensorMap* map, const void* base, int planes, int T, int D) {
+  auto fn = get_encode_fn();
+  if (!fn) return fail(SPECDEC_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(T), static_cast<cuuint64_t>(planes)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(T) * D * 2};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kPage), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SPECDEC_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return SPECDEC_OK;
+}
+
+template <int D, bool VF8, bool TMAP>
+static int ctas_per_sm() {
+  static int cached = 0;
+  if (cached == 0) {
+    using Geo = StageGeom<D, VF8>;
+    auto kern = split_kernel<D, VF8, TMAP>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo::SMEM);
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, Geo::SMEM) != cudaSuccess || n <= 0) n = 1;
+    cached = n;
+  }
+  return cached;
+}
+
+static int q_tile_for(int n_rep) { return n_rep >= kMaxRows ? 1 : kMaxRows / n_rep; }
+
+static int target_items_for(int num_sms, int occ) {
+  // two waves of resident CTAs so ragged item lengths balance; occupancy is
+  // capped at 4 so the workspace size never depends on a device query
+  return num_sms * (occ < 1 ? 1 : (occ > 4 ? 4 : occ)) * 2;
+}
+
+// Records a profiling event; under stream capture it becomes an external
+// event node so the graph's replays can be timed.
+static int record_event(void* ev, cudaStream_t stream) {
+  if (ev == nullptr) return SPECDEC_OK;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) return fail(SPECDEC_ERR_CUDA, "cudaStreamIsCapturing failed");
+  const cudaError_t e = (cs == cudaStreamCaptureStatusActive)
+                            ? cudaEventRecordWithFlags(static_cast<cudaEvent_t>(ev), stream, cudaEventRecordExternal)
+                            : cudaEventRecord(static_cast<cudaEvent_t>(ev), stream);
+  if (e != cudaSuccess) return fail(SPECDEC_ERR_CUDA, "event record: %s", cudaGetErrorString(e));
+  return SPECDEC_OK;
+}
+
+template <int D, bool VF8, bool TMAP>
+static int run_attention(AttnParams p, const CUtensorMap& kmap, const CUtensorMap& vmap, bool build_plan,
+                         cudaStream_t stream, void* ev_begin = nullptr, void* ev_end = nullptr) {
+  using Geo = StageGeom<D, VF8>;
+  if (build_plan) {
+    plan_kernel<<<1, 1024, 0, stream>>>(p);
+    if (int rc = after_launch("plan_kernel")) return rc;
+  }
+  auto kern = split_kernel<D, VF8, TMAP>;
+  (void)ctas_per_sm<D, VF8, TMAP>();  // sets the dynamic smem attribute once
+  if (int rc = record_event(ev_begin, stream)) return rc;
+  kern<<<p.max_items, kThreads, Geo::SMEM, stream>>>(p, kmap, vmap);
+  if (int rc = after_launch("split_kernel")) return rc;
+  if (int rc = record_event(ev_end, stream)) return rc;
+  const int rows_max = p.n_rep * (p.q_tile < p.max_q_len ? p.q_tile : p.max_q_len);
+  dim3 mgrid(p.max_groups, rows_max < kMaxRows ? rows_max : kMaxRows);
+  merge_kernel<D><<<mgrid, 128, 0, stream>>>(p);
+  return after_launch("merge_kernel");
+}
+
+static int fill_workspace(AttnParams& p, void* ws, size_t ws_bytes, int B, int KV, int D, int num_sms, int occ) {
+  const int target = target_items_for(num_sms, occ);
+  const WsLayout w = ws_layout(B, KV, p.max_qtiles, D, target);
+  if (ws == nullptr || ws_bytes < w.total)
+    return fail(SPECDEC_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu required", ws_bytes,
+                w.total);
+  if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return fail(SPECDEC_ERR_INVALID, "workspace must be 256-byte aligned");
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  p.hdr = reinterpret_cast<PlanHeader*>(base);
+  p.items = reinterpret_cast<WorkItem*>(base + w.items);
+  p.groups = reinterpret_cast<GroupInfo*>(base + w.groups);
+  p.p_lse = reinterpret_cast<float*>(base + w.lse);
+  p.p_o = reinterpret_cast<float*>(base + w.po);
+  p.max_items = w.max_items;
+  p.max_groups = w.max_groups;
+  p.target_items = target;
+  return SPECDEC_OK;
+}
+
+static int occupancy_for(int D, bool vf8, bool tmap) {
+  if (D == 128) {
+    if (tmap) return ctas_per_sm<128, false, true>();
+    return vf8 ? ctas_per_sm<128, true, false>() : ctas_per_sm<128, false, false>();
+  }
+  return tmap ? ctas_per_sm<64, false, true>() : ctas_per_sm<64, false, false>();
+}
+
+static int validate_paged(const SpecdecAttnArgs* a) {
+  if (!a) return fail(SPECDEC_ERR_INVALID, "args is NULL");
+  const SpecdecPagedKV& kv = a->kv;
+  const SpecdecBatch& bt = a->batch;
+  if (!a->q || !a->out) return fail(SPECDEC_ERR_INVALID, "q and out must be device pointers");
+  if (!bt.q_row0 || !bt.q_len || !bt.ctx_len) return fail(SPECDEC_ERR_INVALID, "batch arrays must be set");
+  if (!kv.k_pool || !kv.v_pool || !kv.page_table) return fail(SPECDEC_ERR_INVALID, "kv pool pointers must be set");
+  if (bt.num_seqs <= 0 || bt.num_q_heads <= 0 || kv.num_kv_heads <= 0)
+    return fail(SPECDEC_ERR_INVALID, "num_seqs, num_q_heads and num_kv_heads must be positive");
+  if (bt.num_q_heads % kv.num_kv_heads != 0) return fail(SPECDEC_ERR_INVALID, "query heads must divide KV heads");
+  if (bt.num_q_heads / kv.num_kv_heads > kMaxRows)
+    return fail(SPECDEC_ERR_UNSUPPORTED, "more than %d query heads per KV head", kMaxRows);
+  if (kv.head_dim != 64 && kv.head_dim != 128) return fail(SPECDEC_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (kv.v_dtype != SPECDEC_BF16 && kv.v_dtype != SPECDEC_E4M3)
+    return fail(SPECDEC_ERR_UNSUPPORTED, "v_dtype must be SPECDEC_BF16 or SPECDEC_E4M3");
+  if (kv.v_dtype == SPECDEC_E4M3 && kv.head_dim != 128)
+    return fail(SPECDEC_ERR_UNSUPPORTED, "E4M3 V needs head_dim 128 (one scale group per head)");
+  if (kv.v_dtype == SPECDEC_E4M3 && !kv.v_scale) return fail(SPECDEC_ERR_INVALID, "E4M3 V needs v_scale");
+  if (bt.max_q_len <= 0) return fail(SPECDEC_ERR_INVALID, "max_q_len must be positive");
+  if (kv.num_pages <= 0 || kv.max_pages_per_seq <= 0) return fail(SPECDEC_ERR_INVALID, "empty page pool");
+  const uintptr_t al = reinterpret_cast<uintptr_t>(kv.k_pool) | reinterpret_cast<uintptr_t>(kv.v_pool) |
+                       reinterpret_cast<uintptr_t>(kv.v_scale);
+  if (al & 15u) return fail(SPECDEC_ERR_INVALID, "pool pointers must be 16-byte aligned");
+  if ((a->q_stride_head | a->o_stride_head | a->q_stride_tok | a->o_stride_tok) & 3)
+    return fail(SPECDEC_ERR_INVALID, "q/out strides must be multiples of 4 elements (8-byte vectors)");
+  if ((reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->out)) & 7u)
+    return fail(SPECDEC_ERR_INVALID, "q/out must be 8-byte aligned");
+  return SPECDEC_OK;
+}
+
+static AttnParams params_from(const SpecdecAttnArgs* a) {
+  AttnParams p;
+  memset(&p, 0, sizeof(p));
+  p.q = static_cast<const __nv_bfloat16*>(a->q);
+  p.out = static_cast<__nv_bfloat16*>(a->out);
+  p.q_st = a->q_stride_tok;
+  p.q_sh = a->q_stride_head;
+  p.o_st = a->o_stride_tok;
+  p.o_sh = a->o_stride_head;
+  p.q_row0 = a->batch.q_row0;
+  p.q_len = a->batch.q_len;
+  p.ctx_len = a->batch.ctx_len;
+  p.B = a->batch.num_seqs;
+  p.H = a->batch.num_q_heads;
+  p.KV = a->kv.num_kv_heads;
+  p.n_rep = p.H / p.KV;
+  p.max_q_len = a->batch.max_q_len;
+  p.q_tile = q_tile_for(p.n_rep);
+  p.max_qtiles = (p.max_q_len + p.q_tile - 1) / p.q_tile;
+  p.k_pool = static_cast<const uint8_t*>(a->kv.k_pool);
+  p.v_pool = static_cast<const uint8_t*>(a->kv.v_pool);
+  p.v_scale = a->kv.v_scale;
+  p.page_table = a->kv.page_table;
+  p.num_pages = a->kv.num_pages;
+  p.max_pages = a->kv.max_pages_per_seq;
+  p.scale_log2 = a->sm_scale * 1.4426950408889634f;
+  p.status = a->status;
+  return p;
+}
+
+static int paged_entry(const SpecdecAttnArgs* a, cudaStream_t stream, bool plan_only) {
+  if (int rc = validate_paged(a)) return rc;
+  AttnParams p = params_from(a);
+  const int D = a->kv.head_dim;
+  const bool vf8 = a->kv.v_dtype == SPECDEC_E4M3;
+  const int sms = a->num_sms > 0 ? a->num_sms : device_sm_count();
+  if (int rc = fill_workspace(p, a->workspace, a->workspace_bytes, p.B, p.KV, D, sms, occupancy_for(D, vf8, false)))
+    return rc;
+  if (plan_only) {
+    plan_kernel<<<1, 1024, 0, stream>>>(p);
+    return after_launch("plan_kernel");
+  }
+  CUtensorMap dummy;
+  memset(&dummy, 0, sizeof(dummy));
+  const bool build = a->reuse_plan == 0;
+  void* eb = a->split_event_begin;
+  void* ee = a->split_event_end;
+  if (D == 128) {
+    return vf8 ? run_attention<128, true, false>(p, dummy, dummy, build, stream, eb, ee)
+               : run_attention<128, false, false>(p, dummy, dummy, build, stream, eb, ee);
+  }
+  return run_attention<64, false, false>(p, dummy, dummy, build, stream, eb, ee);
+}
+
+}  // namespace sd
+
+using namespace sd;
+
+extern "C" size_t specdec_attn_workspace_bytes(int32_t num_seqs, int32_t num_q_heads, int32_t num_kv_heads,
+                                               int32_t head_dim, int32_t max_q_len, int32_t num_sms) {
+  if (num_seqs <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || max_q_len <= 0 || num_q_heads % num_kv_heads)
+    return 0;
+  const int n_rep = num_q_heads / num_kv_heads;
+  const int qt = q_tile_for(n_rep);
+  const int max_qtiles = (max_q_len + qt - 1) / qt;
+  const int sms = num_sms > 0 ? num_sms : device_sm_count();
+  // occupancy is not known without a device query; size for 4 CTAs per SM (an upper bound)
+  const int target = target_items_for(sms, 4);
+  return ws_layout(num_seqs, num_kv_heads, max_qtiles, head_dim, target).total;
+}
+
+extern "C" int specdec_ragged_plan(const SpecdecAttnArgs* args, specdec_stream_t stream) {
+  return paged_entry(args, reinterpret_cast<cudaStream_t>(stream), true);
+}
+
+extern "C" int specdec_paged_attention(const SpecdecAttnArgs* args, specdec_stream_t stream) {
+  return paged_entry(args, reinterpret_cast<cudaStream_t>(stream), false);
+}
+
+extern "C" size_t specdec_attention_workspace_bytes(int32_t B, int32_t H, int32_t KV, int32_t S, int32_t D,
+                                                    int32_t num_sms) {
+  return specdec_attn_workspace_bytes(B, H, KV, D, S, num_sms);
+}
+
+extern "C" int specdec_attention(const void* q, const void* k, const void* v, void* out, int32_t dtype, int32_t B,
+                                 int32_t H, int32_t KV, int32_t S, int32_t T, int32_t D, void* workspace,
+                                 size_t workspace_bytes, specdec_stream_t stream) {
+  // argument checks of attention_cuda (attention.cu:245-260)
+  if (!q || !k || !v || !out) return fail(SPECDEC_ERR_INVALID, "tensors must be CUDA");
+  if (B <= 0 || H <= 0 || KV <= 0) return fail(SPECDEC_ERR_INVALID, "batch mismatch");
+  if (H % KV != 0) return fail(SPECDEC_ERR_INVALID, "query heads must divide KV heads");
+  if (D != 64 && D != 128) return fail(SPECDEC_ERR_INVALID, "head_dim must be 64 or 128");
+  if (S <= 0 || T <= 0) return fail(SPECDEC_ERR_INVALID, "empty sequence");
+  if (S > T) return fail(SPECDEC_ERR_INVALID, "query rows (%d) exceed keys (%d): early rows would see no key", S, T);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == SPECDEC_F32) {
+    dim3 grid(S, H, B);
+    attn_f32_kernel<<<grid, 128, 0, st>>>(static_cast<const float*>(q), static_cast<const float*>(k),
+                                           static_cast<const float*>(v), static_cast<float*>(out), H, KV, S, T, D,
+                                           1.0f / sqrtf(static_cast<float>(D)));
+    return after_launch("attn_f32_kernel");
+  }
+  if (dtype != SPECDEC_BF16) return fail(SPECDEC_ERR_INVALID, "attention supports float32 and bfloat16");
+  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15u)
+    return fail(SPECDEC_ERR_INVALID, "k and v must be 16-byte aligned for TMA");
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 7u)
+    return fail(SPECDEC_ERR_INVALID, "q and out must be 8-byte aligned");
+  AttnParams p;
+  memset(&p, 0, sizeof(p));
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.q_st = D;
+  p.q_sh = static_cast<int64_t>(S) * D;
+  p.o_st = D;
+  p.o_sh = static_cast<int64_t>(S) * D;
+  p.uni_q_len = S;
+  p.uni_ctx_len = T;
+  p.uni_row_stride = H * S;
+  p.B = B;
+  p.H = H;
+  p.KV = KV;
+  p.n_rep = H / KV;
+  if (p.n_rep > kMaxRows) return fail(SPECDEC_ERR_UNSUPPORTED, "more than %d query heads per KV head", kMaxRows);
+  p.max_q_len = S;
+  p.q_tile = q_tile_for(p.n_rep);
+  p.max_qtiles = (S + p.q_tile - 1) / p.q_tile;
+  p.num_pages = 1;
+  p.max_pages = (T + kPage - 1) / kPage;
+  p.scale_log2 = (1.0f / sqrtf(static_cast<float>(D))) * 1.4426950408889634f;
+  const int sms = device_sm_count();
+  if (int rc = fill_workspace(p, workspace, workspace_bytes, B, KV, D, sms, occupancy_for(D, false, true))) return rc;
+  CUtensorMap kmap, vmap;
+  if (int rc = encode_kv_map(&kmap, k, B * KV, T, D)) return rc;
+  if (int rc = encode_kv_map(&vmap, v, B * KV, T, D)) return rc;
+  if (D == 128) return run_attention<128, false, true>(p, kmap, vmap, true, st);
+  return run_attention<64, false, true>(p, kmap, vmap, true, st);
+}

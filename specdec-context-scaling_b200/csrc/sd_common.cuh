@@ -1,0 +1,186 @@
+// sd_common.cuh -- sm_100a building blocks shared by the kernels of this library:
+// mbarrier / bulk-TMA wrappers, warp-level tensor-core MMA and ldmatrix, FP8
+// conversions, and the page-block layout of the paged KV pool.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/specdec_b200.h"
+
+#define SD_DEV __device__ __forceinline__
+
+namespace sd {
+
+constexpr int kPage = SPECDEC_PAGE_TOKENS;  // tokens per page
+constexpr float kE4M3Max = 448.0f;           // model_self.py:300 E4M3_MAX
+
+// ---------------------------------------------------------------- status word
+SD_DEV void raise_status(int32_t* status, int32_t bits) {
+  if (status != nullptr) atomicOr(status, bits);
+}
+
+// ---------------------------------------------------------------- shared-memory addressing
+SD_DEV uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier
+SD_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+SD_DEV void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+SD_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+SD_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+SD_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+SD_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+SD_DEV uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait for phase `parity` of `bar`.  Gives up after ~1 s of wall time
+// (checked every 256 polls) and returns false; callers then raise
+// SPECDEC_STATUS_TIMEOUT and leave, so a lost arrival can never hang the GPU.
+constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;
+SD_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
+// ---------------------------------------------------------------- bulk TMA (no multicast anywhere)
+// 1-D bulk copy global -> shared, completion counted on `bar` in bytes.
+// src/dst 16-byte aligned, bytes a multiple of 16.
+SD_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+// 3-D tiled tensor load; c0 is the innermost (element) coordinate and must be a
+// multiple of 16 bytes / element size (callers pass 0 or 64 bf16 elements).
+SD_DEV void tma_load_3d(void* dst, const CUtensorMap* map, int32_t c0, int32_t c1, int32_t c2,
+                        uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+SD_DEV void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---------------------------------------------------------------- named barriers
+SD_DEV void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---------------------------------------------------------------- warp MMA (m16n8k16, fp32 accumulate)
+SD_DEV void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+SD_DEV void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+SD_DEV void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+SD_DEV void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// ---------------------------------------------------------------- packing / conversion
+SD_DEV uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);  // .x = lo (low 16 bits)
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+SD_DEV uint32_t pack_f16(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+// Two E4M3 codes (low byte = first element) -> f16x2 (low half = first element).
+// Exact: every E4M3 value, subnormals included, is an f16 normal or zero.
+SD_DEV uint32_t e4m3x2_to_f16x2(uint32_t two_codes) {
+  uint32_t r;
+  const uint16_t v = static_cast<uint16_t>(two_codes & 0xFFFFu);
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(v));
+  return r;
+}
+// Round-to-nearest-even to E4M3 with saturation to +-448.  Returns the code of
+// `first` in the low byte and `second` in the high byte.
+SD_DEV uint32_t f32x2_to_e4m3x2(float first, float second) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(second), "f"(first));
+  return r;
+}
+SD_DEV float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+SD_DEV float fast_log2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// ---------------------------------------------------------------- page-block layouts
+// bf16 K (and bf16 V) page-head block: 16 tokens x D dims, stored as D/64
+// half-tiles of [16 rows][128 bytes]; the 16-byte chunk j of row r is stored at
+// chunk position j ^ (r & 7).  That is exactly what a TMA SWIZZLE_128B load of
+// a {64, 16} box writes to a 1024-byte aligned shared buffer, so pool pages
+// (one bulk copy) and contiguous tensors (tensor-map loads) give the same image.
+// Byte offset of element (row r, dim d) inside the block:
+SD_DEV uint32_t kblock_offset(int r, int d) {
+  const int half = d >> 6;
+  const int chunk = (d & 63) >> 3;
+  return static_cast<uint32_t>(half * 2048 + r * 128 + ((chunk ^ (r & 7)) << 4) + ((d & 7) << 1));
+}
+// Byte offset of 16-byte chunk `c` (dims 8c..8c+7) of row r.
+SD_DEV uint32_t kblock_chunk_offset(int r, int c) {
+  return static_cast<uint32_t>((c >> 3) * 2048 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+// E4M3 V page-head block: [D dims][16 bytes]; token r of dim d is byte
+// d * 16 + vpos(r), where vpos places tokens (2c, 2c+1, 2c+8, 2c+9) in bytes
+// 4c .. 4c+3 so a 32-bit load is the two halves of an m16n8k16 B fragment.
+SD_DEV int vpos(int r) { return (((r & 7) >> 1) << 2) + ((r >> 3) << 1) + (r & 1); }
+
+}  // namespace sd

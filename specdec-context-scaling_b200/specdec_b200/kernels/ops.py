@@ -1,0 +1,414 @@
+"""Operator surface of the B200 build (mirrors specdec/kernels/ops.py:1-76).
+
+The reference dispatches ``backend in {"torch", "cuda", "triton"}``.  This build
+has exactly one implementation per op -- hand-written sm_100a CUDA behind the
+C ABI -- so ``backend`` must be ``"cuda"``; any other value raises
+``ValueError(backend)`` as the reference does for an unknown backend
+(ops.py:39,52,64,76).  There is no CPU or eager fallback.
+
+Beyond the reference's four ops this module exposes the paged decode path:
+``paged_attention``, ``ragged_plan``, ``append_kv``, ``greedy_accept`` and
+``trim_lengths``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+import torch
+
+from .. import _lib
+from ..engine.paged_cache import PagedKVCache
+
+
+def triton_available() -> bool:
+    """Always False: this build ships no Triton kernels (the reference checks the import, ops.py:8-13)."""
+    return False
+
+
+def _backend(backend: str) -> None:
+    if backend != "cuda":
+        raise ValueError(backend)
+
+
+def _lib_handle():
+    from .build import load
+
+    return load().lib
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return _lib.F32
+    if t.dtype == torch.bfloat16:
+        return _lib.BF16
+    return -1
+
+
+def _cos_sin(x, cos, sin):
+    """Flatten cos/sin to (seq, dim) the way the reference op does (ops.py:15-27)."""
+    seq, dim = x.shape[-2], x.shape[-1]
+
+    def flat(t):
+        t = t.to(dtype=x.dtype)
+        while t.ndim > 2 and t.shape[0] == 1:
+            t = t.squeeze(0)
+        if tuple(t.shape) != (seq, dim):
+            t = t.reshape(-1, seq, dim)[-1]
+        return t.contiguous()
+
+    return flat(cos), flat(sin)
+
+
+# ---------------------------------------------------------------------------- reference ops
+def rmsnorm(x, weight, eps: float = 1e-6, backend: str = "cuda"):
+    _backend(backend)
+    from .build import load
+
+    return load().rmsnorm(x.contiguous(), weight.contiguous(), float(eps))
+
+
+def apply_rope(x, cos, sin, backend: str = "cuda"):
+    _backend(backend)
+    cos, sin = _cos_sin(x, cos, sin)
+    from .build import load
+
+    return load().apply_rope(x, cos, sin)
+
+
+def swiglu(gate, up, backend: str = "cuda"):
+    _backend(backend)
+    from .build import load
+
+    return load().swiglu(gate.contiguous(), up.contiguous())
+
+
+def attention(q, k, v, backend: str = "cuda"):
+    """Offset-causal GQA attention, q (B,H,S,D), k/v (B,KV,T,D); row i sees keys j <= i + (T-S)."""
+    _backend(backend)
+    from .build import load
+
+    return load().attention(q.contiguous(), k.contiguous(), v.contiguous())
+
+
+def _attention_cuda(q, k, v):
+    # argument checks of attention_cuda (attention.cu:245-260)
+    if not (q.is_cuda and k.is_cuda and v.is_cuda):
+        raise RuntimeError("tensors must be CUDA")
+    if not (q.is_contiguous() and k.is_contiguous() and v.is_contiguous()):
+        raise RuntimeError("tensors must be contiguous")
+    if not (q.dim() == 4 and k.dim() == 4 and v.dim() == 4):
+        raise RuntimeError("q, k, v are rank-4")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise RuntimeError("dtype mismatch")
+    B, H, S, D = q.shape
+    KV, T = k.shape[1], k.shape[2]
+    if k.shape[0] != B or v.shape[0] != B:
+        raise RuntimeError("batch mismatch")
+    if tuple(v.shape[1:3]) != (KV, T):
+        raise RuntimeError("T mismatch")
+    if k.shape[3] != D or v.shape[3] != D:
+        raise RuntimeError("head_dim mismatch")
+    code = _dtype_code(q)
+    if code < 0:
+        raise RuntimeError("attention supports float32 and bfloat16")
+    lib = _lib_handle()
+    out = torch.empty_like(q)
+    ws_bytes = lib.specdec_attention_workspace_bytes(B, H, KV, S, D, 0) if code == _lib.BF16 else 0
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=q.device)
+    rc = lib.specdec_attention(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), code, B, H, KV, S, T, D,
+        ws.data_ptr(), ws.numel(), _stream(),
+    )
+    _lib.check(rc, "attention")
+    return out
+
+
+def _rmsnorm_cuda(x, weight, eps):
+    if not (x.is_cuda and weight.is_cuda):
+        raise RuntimeError("x must be CUDA")
+    if x.dtype != weight.dtype:
+        raise RuntimeError("x and weight dtype differ")
+    hidden = x.shape[-1]
+    if hidden != weight.numel():
+        raise RuntimeError("weight must match the last dimension")
+    code = _dtype_code(x)
+    if code < 0:
+        raise RuntimeError("rmsnorm supports float32 and bfloat16")
+    out = torch.empty_like(x)
+    rows = x.numel() // hidden if hidden else 0
+    rc = _lib_handle().specdec_rmsnorm(x.data_ptr(), weight.data_ptr(), out.data_ptr(), code, rows, hidden,
+                                       float(eps), _stream())
+    _lib.check(rc, "rmsnorm")
+    return out
+
+
+def _rope_cuda(x, cos, sin):
+    if not (x.is_cuda and cos.is_cuda and sin.is_cuda):
+        raise RuntimeError("tensors must be CUDA")
+    if x.dim() != 4:
+        raise RuntimeError("x is (batch, heads, seq, head_dim)")
+    if not (x.dtype == cos.dtype == sin.dtype):
+        raise RuntimeError("dtype mismatch")
+    B, H, S, D = x.shape
+    if cos.numel() != S * D:
+        raise RuntimeError("cos must be (seq, head_dim)")
+    if sin.numel() != cos.numel():
+        raise RuntimeError("sin shape differs from cos")
+    if x.stride(3) != 1:
+        x = x.contiguous()
+    code = _dtype_code(x)
+    if code < 0:
+        raise RuntimeError("rope supports float32 and bfloat16")
+    out = torch.empty((B, H, S, D), dtype=x.dtype, device=x.device)
+    rc = _lib_handle().specdec_apply_rope(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2), cos.data_ptr(),
+                                          sin.data_ptr(), out.data_ptr(), code, B, H, S, D, _stream())
+    _lib.check(rc, "apply_rope")
+    return out
+
+
+def _swiglu_cuda(gate, up):
+    if not (gate.is_cuda and up.is_cuda):
+        raise RuntimeError("tensors must be CUDA")
+    if gate.shape != up.shape:
+        raise RuntimeError("gate and up shapes differ")
+    if gate.dtype != up.dtype:
+        raise RuntimeError("dtype mismatch")
+    code = _dtype_code(gate)
+    if code < 0:
+        raise RuntimeError("swiglu supports float32 and bfloat16")
+    out = torch.empty_like(gate)
+    rc = _lib_handle().specdec_swiglu(gate.data_ptr(), up.data_ptr(), out.data_ptr(), code, gate.numel(), _stream())
+    _lib.check(rc, "swiglu")
+    return out
+
+
+# ---------------------------------------------------------------------------- paged path
+@dataclass
+class RaggedBatch:
+    """Device description of a ragged batch: query rows, query lengths and KV lengths.
+
+    Query rows of all sequences are packed token-major: row ``i`` of sequence ``b``
+    is packed row ``q_row0[b] + i``.  ``ctx_len[b]`` counts the KV tokens visible
+    to the last query row (the new tokens included)."""
+
+    q_row0: torch.Tensor
+    q_len: torch.Tensor
+    ctx_len: torch.Tensor
+    num_seqs: int
+    max_q_len: int
+    total_rows: int
+
+    @classmethod
+    def from_lengths(cls, q_lens, ctx_lens, device="cuda") -> "RaggedBatch":
+        q_lens = [int(x) for x in q_lens]
+        ctx_lens = [int(x) for x in ctx_lens]
+        if len(q_lens) != len(ctx_lens) or not q_lens:
+            raise ValueError("one q_len and one ctx_len per sequence")
+        row0, acc = [], 0
+        for n in q_lens:
+            row0.append(acc)
+            acc += n
+        t = torch.tensor([row0, q_lens, ctx_lens], dtype=torch.int32).to(device)
+        return cls(t[0].contiguous(), t[1].contiguous(), t[2].contiguous(), len(q_lens), max(max(q_lens), 1), acc)
+
+
+def attn_workspace(batch: RaggedBatch, num_q_heads: int, cache: PagedKVCache) -> torch.Tensor:
+    nbytes = _lib_handle().specdec_attn_workspace_bytes(batch.num_seqs, num_q_heads, cache.num_kv_heads,
+                                                        cache.head_dim, batch.max_q_len, 0)
+    if nbytes == 0:
+        raise ValueError("invalid batch geometry")
+    return torch.empty(nbytes, dtype=torch.uint8, device=cache.device)
+
+
+def _paged_kv(cache: PagedKVCache, layer: int) -> _lib.PagedKV:
+    pool = cache.pools[layer]
+    return _lib.PagedKV(
+        k_pool=pool.k.data_ptr(),
+        v_pool=pool.v.data_ptr(),
+        v_scale=_ptr(pool.v_scale),
+        page_table=cache.page_table.data_ptr(),
+        num_pages=cache.num_pages,
+        num_kv_heads=cache.num_kv_heads,
+        head_dim=cache.head_dim,
+        v_dtype=_lib.E4M3 if cache.v_dtype == "e4m3" else _lib.BF16,
+        max_pages_per_seq=cache.max_pages,
+    )
+
+
+def attn_args(q: torch.Tensor, out: torch.Tensor, cache: PagedKVCache, layer: int, batch: RaggedBatch,
+              workspace: torch.Tensor, *, sm_scale: float | None = None, status: torch.Tensor | None = None,
+              reuse_plan: bool = False, split_events=None) -> _lib.AttnArgs:
+    """Pack the C argument struct of one paged attention call (reusable across calls)."""
+    if q.dim() != 3 or q.dtype != torch.bfloat16:
+        raise ValueError("q must be bf16 (total_rows, num_q_heads, head_dim)")
+    if q.shape[2] != cache.head_dim:
+        raise ValueError("q head_dim differs from the cache")
+    if q.stride(2) != 1 or out.stride(2) != 1:
+        raise ValueError("q/out head_dim must be contiguous")
+    H = q.shape[1]
+    scale = (1.0 / math.sqrt(cache.head_dim)) if sm_scale is None else float(sm_scale)
+    return _lib.AttnArgs(
+        q=q.data_ptr(),
+        out=out.data_ptr(),
+        q_stride_tok=q.stride(0),
+        q_stride_head=q.stride(1),
+        o_stride_tok=out.stride(0),
+        o_stride_head=out.stride(1),
+        batch=_lib.Batch(
+            q_row0=batch.q_row0.data_ptr(),
+            q_len=batch.q_len.data_ptr(),
+            ctx_len=batch.ctx_len.data_ptr(),
+            num_seqs=batch.num_seqs,
+            num_q_heads=H,
+            max_q_len=batch.max_q_len,
+        ),
+        kv=_paged_kv(cache, layer),
+        sm_scale=scale,
+        workspace=workspace.data_ptr(),
+        workspace_bytes=workspace.numel(),
+        status=_ptr(status),
+        reuse_plan=1 if reuse_plan else 0,
+        num_sms=0,
+        split_event_begin=None if split_events is None else _event_handle(split_events[0]),
+        split_event_end=None if split_events is None else _event_handle(split_events[1]),
+    )
+
+
+def _event_handle(ev: torch.cuda.Event) -> int:
+    """Raw cudaEvent_t of a torch event (created on first use)."""
+    if ev.cuda_event == 0:
+        ev.record()
+    return ev.cuda_event
+
+
+def ragged_plan(q, cache: PagedKVCache, batch: RaggedBatch, workspace: torch.Tensor, *, status=None) -> None:
+    """Build the split-KV work list for ``batch`` in ``workspace`` on the device (no host sync)."""
+    args = attn_args(q, q, cache, 0, batch, workspace, status=status)
+    _lib.check(_lib_handle().specdec_ragged_plan(ctypes.byref(args), _stream()), "ragged_plan")
+
+
+def paged_attention(q, cache: PagedKVCache, layer: int, batch: RaggedBatch, *, out=None, workspace=None,
+                    sm_scale=None, status=None, reuse_plan: bool = False, split_events=None):
+    """Decode / verify / ragged attention of packed query rows ``q`` (rows, H, D) over layer ``layer``.
+
+    ``split_events`` (optional pair of torch.cuda.Event with timing) brackets the split-KV kernel."""
+    if not q.is_cuda:
+        raise RuntimeError("tensors must be CUDA")
+    if out is None:
+        out = torch.empty_like(q)
+    if workspace is None:
+        workspace = attn_workspace(batch, q.shape[1], cache)
+        reuse_plan = False
+    args = attn_args(q, out, cache, layer, batch, workspace, sm_scale=sm_scale, status=status,
+                     reuse_plan=reuse_plan, split_events=split_events)
+    _lib.check(_lib_handle().specdec_paged_attention(ctypes.byref(args), _stream()), "paged_attention")
+    return out
+
+
+def append_kv(k_new, v_new, cache: PagedKVCache, layer: int, *, row0, n_new, pos0, max_new: int,
+              len_out=None, status=None) -> None:
+    """Write packed new tokens k_new/v_new (rows, KV, D) bf16 into layer ``layer`` (V quantised when E4M3)."""
+    for t in (k_new, v_new):
+        if t.dtype != torch.bfloat16 or t.dim() != 3 or t.stride(2) != 1:
+            raise ValueError("k_new/v_new must be bf16 (rows, KV, D) with contiguous D")
+    if k_new.stride() != v_new.stride():
+        raise ValueError("k_new and v_new must share strides")
+    pool = cache.pools[layer]
+    args = _lib.AppendArgs(
+        k_new=k_new.data_ptr(),
+        v_new=v_new.data_ptr(),
+        stride_tok=k_new.stride(0),
+        stride_head=k_new.stride(1),
+        row0=row0.data_ptr(),
+        n_new=n_new.data_ptr(),
+        pos0=pos0.data_ptr(),
+        len_out=_ptr(len_out),
+        num_seqs=cache.num_seqs,
+        max_new=int(max_new),
+        k_pool=pool.k.data_ptr(),
+        v_pool=pool.v.data_ptr(),
+        v_scale=_ptr(pool.v_scale),
+        page_table=cache.page_table.data_ptr(),
+        num_pages=cache.num_pages,
+        num_kv_heads=cache.num_kv_heads,
+        head_dim=cache.head_dim,
+        v_dtype=_lib.E4M3 if cache.v_dtype == "e4m3" else _lib.BF16,
+        max_pages_per_seq=cache.max_pages,
+        status=_ptr(status),
+    )
+    _lib.check(_lib_handle().specdec_append_kv(ctypes.byref(args), _stream()), "append_kv")
+
+
+def accept_workspace(num_seqs: int, max_rows: int, vocab: int, device="cuda") -> torch.Tensor:
+    """Zero-filled accept workspace; the kernel leaves its tickets at zero, so it is reusable."""
+    n = _lib_handle().specdec_accept_workspace_bytes(num_seqs, max_rows, vocab)
+    return torch.zeros(max(n, 256), dtype=torch.uint8, device=device)
+
+
+def greedy_accept(logits, *, row0, n_rows, cands, kp, max_rows: int, g=None, m=None, next_token=None,
+                  len_before=None, len_after=None, keep_offset: int = 0, workspace=None, status=None):
+    """argmax of every verify row, accepted prefix length m, next token and rolled-back lengths.
+
+    ``logits`` is (rows, vocab) bf16/f32 with rows of sequence b at ``row0[b] ..``.
+    Returns (g [B, max_rows], m [B], next_token [B]) int32 device tensors."""
+    if logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("logits must be (rows, vocab) with contiguous vocab")
+    code = _dtype_code(logits)
+    if code < 0:
+        raise ValueError("logits must be bf16 or f32")
+    B = int(kp.numel())
+    max_cands = int(cands.shape[1])
+    dev = logits.device
+    if g is None:
+        g = torch.empty(B, max_rows, dtype=torch.int32, device=dev)
+    if m is None:
+        m = torch.empty(B, dtype=torch.int32, device=dev)
+    if next_token is None:
+        next_token = torch.empty(B, dtype=torch.int32, device=dev)
+    if workspace is None:
+        workspace = accept_workspace(B, max_rows, logits.shape[1], dev)
+    args = _lib.AcceptArgs(
+        logits=logits.data_ptr(),
+        logits_dtype=code,
+        row_stride=logits.stride(0),
+        vocab=logits.shape[1],
+        row0=row0.data_ptr(),
+        n_rows=n_rows.data_ptr(),
+        cands=cands.data_ptr(),
+        kp=kp.data_ptr(),
+        num_seqs=B,
+        max_rows=int(max_rows),
+        max_cands=max_cands,
+        g=g.data_ptr(),
+        m=m.data_ptr(),
+        next_token=next_token.data_ptr(),
+        len_before=_ptr(len_before),
+        len_after=_ptr(len_after),
+        keep_offset=int(keep_offset),
+        workspace=workspace.data_ptr(),
+        workspace_bytes=workspace.numel(),
+        status=_ptr(status),
+    )
+    _lib.check(_lib_handle().specdec_greedy_accept(ctypes.byref(args), _stream()), "greedy_accept")
+    return g, m, next_token
+
+
+def trim_lengths(cur_len, new_len, out=None, status=None):
+    """Device rollback: out[b] = new_len[b] if 0 < new_len[b] <= cur_len[b] else cur_len[b] (+ status bit)."""
+    if out is None:
+        out = torch.empty_like(cur_len)
+    rc = _lib_handle().specdec_trim(cur_len.data_ptr(), new_len.data_ptr(), out.data_ptr(), int(cur_len.numel()),
+                                    _ptr(status), _stream())
+    _lib.check(rc, "trim")
+    return out

@@ -1,0 +1,103 @@
+"""GPU: quantise-on-append writes exactly the oracle's pool bytes (FP8 codes, scales,
+bf16 K/V, page placement) -- the reference's quantize_kv_fp8 contract, bit for bit."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_helpers import cache_from_kv, oracle_pools, seeded_kv, u16
+from oracle import paged as opg
+
+pytestmark = pytest.mark.gpu
+
+
+def _ops():
+    from specdec_b200.kernels import ops
+
+    return ops
+
+
+@pytest.mark.parametrize("fp8,D", [(True, 128), (False, 128), (False, 64)])
+def test_append_matches_oracle_pools(fp8, D):
+    ops = _ops()
+    KV = 2
+    before = [1, 13, 100, 16, 250]
+    n_new = [16, 5, 1, 33, 0]
+    cap = 320
+    ks_old, vs_old = seeded_kv(before, KV, D, seed=21, fp8=fp8)
+    ks_new, vs_new = seeded_kv(n_new, KV, D, seed=22, fp8=fp8)
+    cache, _ = cache_from_kv(ks_old, vs_old, KV, D, fp8=fp8, seed=23, capacity=cap)
+    # packed new rows (rows, KV, D)
+    k_rows = torch.cat([k.permute(1, 0, 2) for k in ks_new], dim=0).contiguous().cuda()
+    v_rows = torch.cat([v.permute(1, 0, 2) for v in vs_new], dim=0).contiguous().cuda()
+    row0 = torch.tensor(np.cumsum([0] + n_new[:-1]), dtype=torch.int32, device="cuda")
+    nn = torch.tensor(n_new, dtype=torch.int32, device="cuda")
+    pos0 = torch.tensor(before, dtype=torch.int32, device="cuda")
+    len_out = torch.zeros(len(before), dtype=torch.int32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.append_kv(k_rows, v_rows, cache, 0, row0=row0, n_new=nn, pos0=pos0, max_new=max(n_new), len_out=len_out,
+                  status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert len_out.cpu().tolist() == [a + b for a, b in zip(before, n_new)]
+
+    ks_all = [torch.cat([a, b], dim=1) for a, b in zip(ks_old, ks_new)]
+    vs_all = [torch.cat([a, b], dim=1) for a, b in zip(vs_old, vs_new)]
+    pt = cache.page_table.cpu().numpy()
+    kp, vp, sp, _ = oracle_pools(ks_all, vs_all, pt, cache.num_pages, fp8)
+    pool = cache.pools[0]
+    np.testing.assert_array_equal(pool.k.cpu().view(torch.int16).numpy().view(np.uint16), kp)
+    if fp8:
+        np.testing.assert_array_equal(pool.v.cpu().numpy(), vp)
+        np.testing.assert_array_equal(pool.v_scale.cpu().numpy().view(np.uint32), sp.view(np.uint32))
+    else:
+        np.testing.assert_array_equal(pool.v.cpu().view(torch.int16).numpy().view(np.uint16), vp)
+
+
+def test_append_full_history_fp8_8k():
+    """Quantise an 8192-token V history (the FP8 config) and gather it back bit-exactly."""
+    ops = _ops()
+    from oracle import fp8 as ofp8
+    from specdec_b200.engine.paged_cache import PagedKVCache
+
+    T, KV, D = 8192, 2, 128
+    ks, vs = seeded_kv([T], KV, D, seed=31, fp8=True)
+    cache = PagedKVCache.allocate(1, 1, KV, D, T, v_dtype="e4m3", device="cuda", page_order_seed=5)
+    ops.append_kv(ks[0].permute(1, 0, 2).contiguous().cuda(), vs[0].permute(1, 0, 2).contiguous().cuda(), cache, 0,
+                  row0=torch.zeros(1, dtype=torch.int32, device="cuda"),
+                  n_new=torch.tensor([T], dtype=torch.int32, device="cuda"),
+                  pos0=torch.zeros(1, dtype=torch.int32, device="cuda"), max_new=T)
+    got = cache.gather_layer(0, 0, T)
+    codes, scale = ofp8.quantize_v(vs[0].float().numpy())
+    np.testing.assert_array_equal(got["v"][0].view(torch.uint8).cpu().numpy(), codes)
+    np.testing.assert_array_equal(got["v_scale"][0, :, :, 0].cpu().numpy().view(np.uint32),
+                                  scale[..., 0].view(np.uint32))
+    assert torch.equal(got["k"][0].cpu().view(torch.int16), ks[0].view(torch.int16))
+
+
+def test_append_bad_position_sets_status():
+    from specdec_b200 import _lib
+
+    ops = _ops()
+    ks, vs = seeded_kv([4], 2, 128, seed=3, fp8=True)
+    cache, _ = cache_from_kv(ks, vs, 2, 128, fp8=True, seed=4, capacity=16)
+    k = torch.zeros(1, 2, 128, dtype=torch.bfloat16, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    one = torch.ones(1, dtype=torch.int32, device="cuda")
+    ops.append_kv(k, k, cache, 0, row0=torch.zeros_like(one), n_new=one, pos0=one * 16, max_new=1, status=status)
+    assert int(status.item()) & _lib.STATUS_PAGE_OVERFLOW
+
+
+def test_gather_layer_round_trip():
+    ks, vs = seeded_kv([77, 3], 2, 128, seed=9, fp8=False)
+    cache, _ = cache_from_kv(ks, vs, 2, 128, fp8=False, seed=10, capacity=80)
+    for b, n in enumerate([77, 3]):
+        got = cache.gather_layer(0, b, n)
+        assert torch.equal(got["k"][0].cpu().view(torch.int16), ks[b].view(torch.int16))
+        assert torch.equal(got["v"][0].cpu().view(torch.int16), vs[b].view(torch.int16))
+    k_np, _, _ = opg.gather(cache.pools[0].k.cpu().view(torch.int16).numpy().view(np.uint16),
+                            cache.pools[0].v.cpu().view(torch.int16).numpy().view(np.uint16), None,
+                            cache.page_table.cpu().numpy(), 0, 77)
+    np.testing.assert_array_equal(k_np, u16(ks[0]))

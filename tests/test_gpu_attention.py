@@ -1,0 +1,156 @@
+"""GPU parity of the attention kernels against the oracle and the reference's golden outputs.
+
+Tolerance (north star): |got - ref| <= 1e-2 + 2e-2 * |ref| elementwise for bf16 outputs,
+against both the eager reference (bf16 scores) and its fp32 formula; 1e-4 absolute for
+the fp32 contiguous op (sample_experiment.py:21)."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from gpu_helpers import assert_close_attention, build_cache, oracle_rows
+from oracle import attention as oatt
+
+pytestmark = pytest.mark.gpu
+
+
+def _ops():
+    from specdec_b200.kernels import ops
+
+    return ops
+
+
+def test_contiguous_attention_matches_golden(golden):
+    ops = _ops()
+    for name, case in golden["attention"].items():
+        q, k, v = (case[x].cuda() for x in ("q", "k", "v"))
+        got = ops.attention(q, k, v, backend="cuda").cpu()
+        if q.dtype == torch.float32:
+            torch.testing.assert_close(got, case["fp32"], rtol=0, atol=1e-4, msg=name)
+            continue
+        assert_close_attention(got, case["eager"], f"{name} vs eager")
+        assert_close_attention(got, case["fp32"], f"{name} vs fp32")
+
+
+@pytest.mark.parametrize("S,T", [(1, 1), (1, 15), (1, 16), (1, 17), (5, 5), (5, 21), (2, 300), (5, 2048), (64, 64)])
+@pytest.mark.parametrize("H,KV,D", [(12, 2, 128), (14, 2, 64)])
+def test_contiguous_attention_shapes(S, T, H, KV, D):
+    ops = _ops()
+    g = torch.Generator().manual_seed(S * 1000 + T + H)
+    q = torch.randn(2, H, S, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(2, KV, T, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(2, KV, T, D, generator=g).to(torch.bfloat16)
+    got = ops.attention(q.cuda(), k.cuda(), v.cuda()).cpu()
+    assert_close_attention(got, oatt.attention_fp32(q, k, v), f"S={S} T={T}")
+    assert_close_attention(got, oatt.eager_attention(q, k, v), f"S={S} T={T} eager")
+
+
+def _paged_case(lens, q_lens, H, KV, D, fp8, seed):
+    ops = _ops()
+    cache, ks, vrefs = build_cache(lens, KV, D, fp8=fp8, seed=seed)
+    batch = ops.RaggedBatch.from_lengths(q_lens, lens)
+    g = torch.Generator().manual_seed(seed + 7)
+    q = torch.randn(batch.total_rows, H, D, generator=g).to(torch.bfloat16)
+    out = ops.paged_attention(q.cuda(), cache, 0, batch)
+    torch.cuda.synchronize()
+    return out.cpu(), oracle_rows(q, ks, vrefs, q_lens), q, ks, vrefs
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+@pytest.mark.parametrize("S", [1, 5])
+@pytest.mark.parametrize("T", [5, 16, 17, 100, 2048, 8192])
+def test_paged_attention_single_sequence(fp8, S, T):
+    got, ref, *_ = _paged_case([T], [S], 12, 2, 128, fp8, seed=T * 10 + S)
+    assert_close_attention(got, ref, f"fp8={fp8} S={S} T={T}")
+
+
+@pytest.mark.parametrize("S", [1, 5])
+def test_paged_attention_draft_geometry(S):
+    got, ref, *_ = _paged_case([333, 64], [S, S], 14, 2, 64, False, seed=3 + S)
+    assert_close_attention(got, ref, f"14:2 d64 S={S}")
+
+
+def test_paged_attention_matches_eager_reference_fp8():
+    got, _, q, ks, vrefs = _paged_case([2048], [5], 12, 2, 128, True, seed=99)
+    ref = oracle_rows(q, ks, vrefs, [5], eager=True)
+    assert_close_attention(got, ref, "fp8 vs eager")
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_ragged_batch_mixed_rows(fp8):
+    """Mixed decode (q=1) and verify (q=5) rows, ragged lengths, one idle sequence, one launch."""
+    rng = torch.Generator().manual_seed(5)
+    lens = [int(x) for x in torch.randint(1, 3000, (15,), generator=rng)] + [40]
+    q_lens = [1 if i % 2 else 5 for i in range(15)] + [0]
+    lens = [max(n, q) for n, q in zip(lens, q_lens)]
+    got, ref, *_ = _paged_case(lens, q_lens, 12, 2, 128, fp8, seed=17)
+    assert_close_attention(got, ref, f"ragged fp8={fp8}")
+
+
+def test_plan_reuse_across_layers():
+    """One plan serves every layer: reuse_plan=True gives the same output as a fresh plan."""
+    ops = _ops()
+    lens, q_lens = [700, 1500, 64], [5, 1, 5]
+    cache, ks, vrefs = build_cache(lens, 2, 128, fp8=True, seed=8, num_layers=2)
+    batch = ops.RaggedBatch.from_lengths(q_lens, lens)
+    q = torch.randn(batch.total_rows, 12, 128, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16).cuda()
+    ws = ops.attn_workspace(batch, 12, cache)
+    ops.ragged_plan(q, cache, batch, ws)
+    a = ops.paged_attention(q, cache, 1, batch, workspace=ws, reuse_plan=True)
+    b = ops.paged_attention(q, cache, 1, batch)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+def test_bad_page_id_sets_status_without_fault():
+    """A corrupted page table (host-side) is caught by the producer's bounds check."""
+    from specdec_b200 import _lib
+
+    ops = _ops()
+    cache, ks, vrefs = build_cache([100], 2, 128, fp8=False, seed=4)
+    cache.page_table[0, 2] = cache.num_pages + 5
+    batch = ops.RaggedBatch.from_lengths([1], [100])
+    q = torch.randn(1, 12, 128, device="cuda", dtype=torch.bfloat16)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.paged_attention(q, cache, 0, batch, status=status)
+    assert int(status.item()) & _lib.STATUS_BAD_PAGE
+
+
+def test_length_overflow_sets_status():
+    from specdec_b200 import _lib
+
+    ops = _ops()
+    cache, *_ = build_cache([32], 2, 128, fp8=False, seed=6)
+    batch = ops.RaggedBatch.from_lengths([1, 5], [10 ** 6, 2])  # beyond the page table; ctx < q_len
+    from specdec_b200.engine.paged_cache import PagedKVCache
+
+    big = PagedKVCache.allocate(1, 2, 2, 128, 32, device="cuda")
+    q = torch.zeros(6, 12, 128, device="cuda", dtype=torch.bfloat16)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.paged_attention(q, big, 0, batch, status=status)
+    s = int(status.item())
+    assert s & _lib.STATUS_PAGE_OVERFLOW and s & _lib.STATUS_BAD_LENGTH
+    del cache
+
+
+def test_cuda_graph_replay_matches_eager():
+    ops = _ops()
+    lens, q_lens = [1000, 2500], [5, 5]
+    cache, ks, vrefs = build_cache(lens, 2, 128, fp8=True, seed=12)
+    batch = ops.RaggedBatch.from_lengths(q_lens, lens)
+    q = torch.randn(batch.total_rows, 12, 128, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).cuda()
+    ws = ops.attn_workspace(batch, 12, cache)
+    out = torch.empty_like(q)
+    ops.paged_attention(q, cache, 0, batch, out=out, workspace=ws)  # warm-up outside capture
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            ops.paged_attention(q, cache, 0, batch, out=out, workspace=ws)
+    torch.cuda.current_stream().wait_stream(s)
+    out.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert_close_attention(out.cpu(), oracle_rows(q.cpu(), ks, vrefs, q_lens), "graph replay")
