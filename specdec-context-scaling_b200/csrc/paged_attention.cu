@@ -48,9 +48,6 @@ struct PlanHeader {
 static_assert(sizeof(PlanHeader) == 256, "plan header is 256 bytes");
 
 constexpr int kMaxRows = 64;  // query rows (n_rep x query positions) per work item
-constexpr int kConsumerWarps = 4;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kStages = 8;
 
 struct WsLayout {
   size_t items, groups, lse, po, total;
@@ -155,6 +152,7 @@ SD_DEV int block_exclusive_scan(int v, int& total, int* s_warp) {
 __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
   __shared__ int s_warp[32];
   __shared__ long long s_total;
+  __shared__ int s_first[1024], s_pages[1024], s_nq[1024];
   const int ngroups = p.max_groups;
   if (threadIdx.x == 0) s_total = 0;
   __syncthreads();
@@ -170,7 +168,15 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
                                          static_cast<unsigned long long>(local));
   __syncthreads();
   const long long total = s_total;
-  int pps = static_cast<int>((total + p.target_items - 1) / p.target_items);
+  // pages per split: one wave of CTAs (one per SM) while that keeps a CTA at <= 64
+  // pages; above that ~4 waves of >= 64-page items so ragged lengths balance.
+  // Either way num_items <= total / pps + groups <= 4 * num_sms + groups = max_items.
+  const int sms = p.target_items / 4;
+  int pps = static_cast<int>((total + sms - 1) / sms);
+  if (pps > 64) {
+    pps = static_cast<int>((total + 4LL * sms - 1) / (4LL * sms));
+    pps = max(pps, 64);
+  }
   pps = max(pps, 1);
 
   int carry = 0;
@@ -191,19 +197,37 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
       g.nq = nq;
       g.pad0 = g.pad1 = 0;
       p.groups[gi] = g;
-      for (int s = 0; s < n; ++s) {
-        WorkItem it;
-        it.b = b;
-        it.h = h;
-        it.q0 = q0;
-        it.nq = nq;
-        it.page_begin = s * pps;
-        it.page_end = min((s + 1) * pps, pages);
-        it.group = gi;
-        it.nsplit = n;
-        p.items[first + s] = it;
-      }
     }
+    // items of this chunk of groups, written in parallel: item i belongs to the
+    // last group whose first item is <= i (empty groups never match)
+    s_first[threadIdx.x] = (gi < ngroups) ? first - carry : 0x7fffffff;
+    s_pages[threadIdx.x] = pages;
+    s_nq[threadIdx.x] = nq;
+    __syncthreads();
+    for (int i = threadIdx.x; i < chunk_total; i += blockDim.x) {
+      int lo = 0, hi = blockDim.x - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_first[mid] <= i) lo = mid; else hi = mid - 1;
+      }
+      const int g2 = base + lo;
+      const int s = i - s_first[lo];
+      const int pg = s_pages[lo];
+      const int per_b = p.max_qtiles * p.KV;
+      const int b2 = g2 / per_b;
+      const int rem = g2 - b2 * per_b;
+      WorkItem it;
+      it.b = b2;
+      it.h = rem % p.KV;
+      it.q0 = (rem / p.KV) * p.q_tile;
+      it.nq = s_nq[lo];
+      it.page_begin = s * pps;
+      it.page_end = min((s + 1) * pps, pg);
+      it.group = g2;
+      it.nsplit = (pg + pps - 1) / pps;
+      p.items[carry + i] = it;
+    }
+    __syncthreads();
     carry += chunk_total;
   }
   if (threadIdx.x == 0) {
@@ -215,352 +239,15 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
 }
 
 // ---------------------------------------------------------------- split kernel
-template <int D, bool VF8>
-struct StageGeom {
-  static constexpr int KB = D * 32;                 // 16 tokens x D x bf16
-  static constexpr int VB = VF8 ? D * 16 : D * 32;  // E4M3 codes or bf16
-  static constexpr int SB = VF8 ? 64 : 0;           // 16 fp32 scales
-  static constexpr int BYTES = ((KB + VB + SB + 1023) / 1024) * 1024;
-  static constexpr int SMEM = kStages * BYTES + 1024;  // + alignment slack
-  static constexpr int MERGE_ROW = D + 8;              // padded fp32 row in the merge area
-  static constexpr int MERGE_WARP = 16 * MERGE_ROW * 4 + 256;
-  static_assert(kConsumerWarps * MERGE_WARP <= kStages * BYTES, "merge area fits in the ring");
-};
-
-template <int D, bool VF8, bool TMAP>
-__global__ void __launch_bounds__(kThreads) split_kernel(const AttnParams p,
-                                                         const __grid_constant__ CUtensorMap kmap,
-                                                         const __grid_constant__ CUtensorMap vmap) {
-  using Geo = StageGeom<D, VF8>;
-  constexpr int NKK = D / 16;  // k-steps of QK^T
-  constexpr int NNT = D / 8;   // n-tiles of PV
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t full_bar[kStages];
-  __shared__ uint64_t empty_bar[kStages];
-  __shared__ int s_abort;
-  __shared__ int s_issued;
-
-  if (static_cast<int>(blockIdx.x) >= p.hdr->num_items) return;  // uniform per CTA
-  const WorkItem it = p.items[blockIdx.x];
-  const int R = p.n_rep * it.nq;
-  int G = (R + 15) >> 4;
-  if (G == 3) G = 4;
-  const int KS = kConsumerWarps / G;
-  const int npages = it.page_end - it.page_begin;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], G);
-    }
-    s_abort = 0;
-    s_issued = 0;
-    fence_barrier_init();
-  }
-  __syncthreads();
-
-  // per-thread softmax state (consumers)
-  float o[NNT][4];
-  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f, sref = 0.f;
-  const int gq = lane >> 2, cq = lane & 3;
-  const int g = warp % G;
-
-  if (warp == kConsumerWarps) {
-    // ------------------------------------------------ producer: one elected lane
-    if (lane == 0) {
-      if (TMAP) {
-        prefetch_tmap(&kmap);
-        prefetch_tmap(&vmap);
-      }
-      int li = 0;
-      for (; li < npages; ++li) {
-        const int slot = li % kStages;
-        if (li >= kStages) {
-          if (!mbar_wait(&empty_bar[slot], ((li / kStages) - 1) & 1)) {
-            raise_status(p.status, SPECDEC_STATUS_TIMEOUT);
-            atomicExch(&s_abort, 1);
-            break;
-          }
-        }
-        if (*reinterpret_cast<volatile int*>(&s_abort)) break;
-        uint8_t* st = smem + slot * Geo::BYTES;
-        const int blk = it.page_begin + li;
-        if (TMAP) {
-          mbar_arrive_expect_tx(&full_bar[slot], Geo::KB + Geo::VB);
-          const int plane = it.b * p.KV + it.h;
-#pragma unroll
-          for (int hf = 0; hf < D / 64; ++hf) {
-            tma_load_3d(st + hf * 2048, &kmap, hf * 64, blk * kPage, plane, &full_bar[slot]);
-            tma_load_3d(st + Geo::KB + hf * 2048, &vmap, hf * 64, blk * kPage, plane, &full_bar[slot]);
-          }
-        } else {
-          const int page = __ldg(p.page_table + static_cast<int64_t>(it.b) * p.max_pages + blk);
-          if (page < 0 || page >= p.num_pages) {
-            raise_status(p.status, SPECDEC_STATUS_BAD_PAGE);
-            mbar_arrive(&full_bar[slot]);  // complete the phase without data
-            continue;
-          }
-          const int64_t ph = static_cast<int64_t>(page) * p.KV + it.h;
-          mbar_arrive_expect_tx(&full_bar[slot], Geo::KB + Geo::VB + Geo::SB);
-          bulk_g2s(st, p.k_pool + ph * Geo::KB, Geo::KB, &full_bar[slot]);
-          bulk_g2s(st + Geo::KB, p.v_pool + ph * Geo::VB, Geo::VB, &full_bar[slot]);
-          if (VF8) bulk_g2s(st + Geo::KB + Geo::VB, p.v_scale + ph * kPage, Geo::SB, &full_bar[slot]);
-        }
-      }
-      s_issued = li;
-    }
-  } else {
-    // ------------------------------------------------ consumers
-    const int ks = warp / G;
-    const int qlen = seq_q_len(p, it.b);
-    const int ctx = seq_ctx_len(p, it.b);
-    const int row0 = seq_row0(p, it.b);
-    const int ra = g * 16 + gq, rb = ra + 8;
-    int lim_a = -1, lim_b = -1;
-    uint32_t qf[NKK][4];
-    {
-      const __nv_bfloat16* qa = nullptr;
-      const __nv_bfloat16* qb = nullptr;
-      if (ra < R) {
-        const int hh = ra / it.nq, qi = it.q0 + ra % it.nq;
-        qa = p.q + static_cast<int64_t>(row0 + qi) * p.q_st + static_cast<int64_t>(it.h * p.n_rep + hh) * p.q_sh;
-        lim_a = qi + ctx - qlen;
-      }
-      if (rb < R) {
-        const int hh = rb / it.nq, qi = it.q0 + rb % it.nq;
-        qb = p.q + static_cast<int64_t>(row0 + qi) * p.q_st + static_cast<int64_t>(it.h * p.n_rep + hh) * p.q_sh;
-        lim_b = qi + ctx - qlen;
-      }
-#pragma unroll
-      for (int kk = 0; kk < NKK; ++kk) {
-        const int d0 = kk * 16 + 2 * cq;
-        qf[kk][0] = qa ? *reinterpret_cast<const uint32_t*>(qa + d0) : 0u;
-        qf[kk][1] = qb ? *reinterpret_cast<const uint32_t*>(qb + d0) : 0u;
-        qf[kk][2] = qa ? *reinterpret_cast<const uint32_t*>(qa + d0 + 8) : 0u;
-        qf[kk][3] = qb ? *reinterpret_cast<const uint32_t*>(qb + d0 + 8) : 0u;
-      }
-    }
-#pragma unroll
-    for (int nt = 0; nt < NNT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
-
-    for (int li = ks; li < npages; li += KS) {
-      const int slot = li % kStages;
-      // every lane polls; the give-up decision is made warp-wide so the warp
-      // leaves the loop together (the shuffles below need all 32 lanes)
-      if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[slot], (li / kStages) & 1))) {
-        raise_status(p.status, SPECDEC_STATUS_TIMEOUT);
-        atomicExch(&s_abort, 1);
-        break;
-      }
-      const uint32_t kb = smem_u32(smem + slot * Geo::BYTES);
-      const uint32_t vb = kb + Geo::KB;
-
-      // S = Q K^T for this block's 16 keys: tile 0 = keys 0-7, tile 1 = keys 8-15
-      float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
-      {
-        const int key = (lane & 7) + ((lane >> 4) << 3);
-        const int csel = (lane >> 3) & 1;
-#pragma unroll
-        for (int kk = 0; kk < NKK; ++kk) {
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4(kb + kblock_chunk_offset(key, 2 * kk + csel), b0, b1, b2, b3);
-          mma_bf16(s0, qf[kk], b0, b1);
-          mma_bf16(s1, qf[kk], b2, b3);
-        }
-      }
-      const int key0 = (it.page_begin + li) * kPage;
-      const int ka = key0 + 2 * cq;
-      float xa[4] = {s0[0], s0[1], s1[0], s1[1]};
-      float xb[4] = {s0[2], s0[3], s1[2], s1[3]};
-      const int kx[4] = {ka, ka + 1, ka + 8, ka + 9};
-      float mxa = -INFINITY, mxb = -INFINITY;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        xa[e] = (kx[e] <= lim_a) ? xa[e] * p.scale_log2 : -INFINITY;
-        xb[e] = (kx[e] <= lim_b) ? xb[e] * p.scale_log2 : -INFINITY;
-        mxa = fmaxf(mxa, xa[e]);
-        mxb = fmaxf(mxb, xb[e]);
-      }
-      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));
-      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 2));
-      mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
-      mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
-      const float mna = fmaxf(m_a, mxa), mnb = fmaxf(m_b, mxb);
-      const float ua = (mna == -INFINITY) ? 0.f : mna;
-      const float ub = (mnb == -INFINITY) ? 0.f : mnb;
-      float alpha_a = fast_exp2(m_a - ua), alpha_b = fast_exp2(m_b - ub);
-      m_a = mna;
-      m_b = mnb;
-      float pa[4], pb[4];
-      float suma = 0.f, sumb = 0.f;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        pa[e] = fast_exp2(xa[e] - ua);
-        pb[e] = fast_exp2(xb[e] - ub);
-        suma += pa[e];
-        sumb += pb[e];
-      }
-      l_a = l_a * alpha_a + suma;
-      l_b = l_b * alpha_b + sumb;
-
-      uint32_t pf[4];
-      if (VF8) {
-        // fold the per-token V scales into P; keep the accumulator in units of
-        // the running maximum scale `sref` so P * s / sref stays in [0, 1].
-        const float* sc = reinterpret_cast<const float*>(smem + slot * Geo::BYTES + Geo::KB + Geo::VB);
-        float sl = (key0 + (lane & 15) < ctx) ? sc[lane & 15] : 0.f;
-        sl = fmaxf(sl, __shfl_xor_sync(0xffffffffu, sl, 8));
-        sl = fmaxf(sl, __shfl_xor_sync(0xffffffffu, sl, 4));
-        sl = fmaxf(sl, __shfl_xor_sync(0xffffffffu, sl, 2));
-        sl = fmaxf(sl, __shfl_xor_sync(0xffffffffu, sl, 1));
-        const float nref = fmaxf(sref, sl);
-        if (nref > sref) {
-          const float ratio = sref / nref;  // 0 on the first block: o is still zero
-          alpha_a *= ratio;
-          alpha_b *= ratio;
-          sref = nref;
-        }
-        const float inv = (sref > 0.f) ? 1.f / sref : 0.f;
-        const float2 s01 = *reinterpret_cast<const float2*>(sc + 2 * cq);
-        const float2 s89 = *reinterpret_cast<const float2*>(sc + 8 + 2 * cq);
-        const float sk[4] = {s01.x * inv, s01.y * inv, s89.x * inv, s89.y * inv};
-        pf[0] = pack_f16(pa[0] * sk[0], pa[1] * sk[1]);
-        pf[1] = pack_f16(pb[0] * sk[0], pb[1] * sk[1]);
-        pf[2] = pack_f16(pa[2] * sk[2], pa[3] * sk[3]);
-        pf[3] = pack_f16(pb[2] * sk[2], pb[3] * sk[3]);
-      } else {
-        pf[0] = pack_bf16(pa[0], pa[1]);
-        pf[1] = pack_bf16(pb[0], pb[1]);
-        pf[2] = pack_bf16(pa[2], pa[3]);
-        pf[3] = pack_bf16(pb[2], pb[3]);
-      }
-      if (__any_sync(0xffffffffu, alpha_a != 1.f || alpha_b != 1.f)) {
-#pragma unroll
-        for (int nt = 0; nt < NNT; ++nt) {
-          o[nt][0] *= alpha_a;
-          o[nt][1] *= alpha_a;
-          o[nt][2] *= alpha_b;
-          o[nt][3] *= alpha_b;
-        }
-      }
-      // O += P V
-      if (VF8) {
-        const uint8_t* vrow = smem + slot * Geo::BYTES + Geo::KB;
-#pragma unroll
-        for (int nt = 0; nt < NNT; ++nt) {
-          const uint32_t w = *reinterpret_cast<const uint32_t*>(vrow + (nt * 8 + gq) * 16 + 4 * cq);
-          mma_f16(o[nt], pf, e4m3x2_to_f16x2(w), e4m3x2_to_f16x2(w >> 16));
-        }
-      } else {
-        const int key = (lane & 7) + (((lane >> 3) & 1) << 3);
-        const int csel = lane >> 4;
-#pragma unroll
-        for (int nt = 0; nt < NNT; nt += 2) {
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4_trans(vb + kblock_chunk_offset(key, nt + csel), b0, b1, b2, b3);
-          mma_bf16(o[nt], pf, b0, b1);
-          mma_bf16(o[nt + 1], pf, b2, b3);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty_bar[slot]);
-    }
-    l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
-    l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
-    l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
-    l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
-  }
-  __syncthreads();  // (A) every page consumed, every copy landed; the ring is free
-
-  const bool aborted = *reinterpret_cast<volatile int*>(&s_abort) != 0;
-  if (!aborted && warp < kConsumerWarps) {
-    uint8_t* area = smem + warp * Geo::MERGE_WARP;
-    float* om = reinterpret_cast<float*>(area);
-    float* mm = reinterpret_cast<float*>(area + 16 * Geo::MERGE_ROW * 4);
-    float* lm = mm + 16;
-    const float f = VF8 ? sref : 1.f;
-#pragma unroll
-    for (int nt = 0; nt < NNT; ++nt) {
-      const int d = nt * 8 + 2 * cq;
-      *reinterpret_cast<float2*>(om + gq * Geo::MERGE_ROW + d) = make_float2(o[nt][0] * f, o[nt][1] * f);
-      *reinterpret_cast<float2*>(om + (gq + 8) * Geo::MERGE_ROW + d) = make_float2(o[nt][2] * f, o[nt][3] * f);
-    }
-    if (cq == 0) {
-      mm[gq] = m_a;
-      mm[gq + 8] = m_b;
-      lm[gq] = l_a;
-      lm[gq + 8] = l_b;
-    }
-  }
-  __syncthreads();  // (B)
-
-  if (!aborted && threadIdx.x < kConsumerWarps * 32) {
-    const int qlen = seq_q_len(p, it.b);
-    (void)qlen;
-    const int row0 = seq_row0(p, it.b);
-    const int units = R * (D / 4);
-    for (int u = threadIdx.x; u < units; u += kConsumerWarps * 32) {
-      const int r = u / (D / 4);
-      const int d = (u - r * (D / 4)) * 4;
-      const int rg = r >> 4, rr = r & 15;
-      float M = -INFINITY;
-      for (int ks = 0; ks < KS; ++ks) {
-        const float* mm = reinterpret_cast<const float*>(smem + (rg + G * ks) * Geo::MERGE_WARP +
-                                                         16 * Geo::MERGE_ROW * 4);
-        M = fmaxf(M, mm[rr]);
-      }
-      float L = 0.f;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (M != -INFINITY) {
-        for (int ks = 0; ks < KS; ++ks) {
-          const uint8_t* area = smem + (rg + G * ks) * Geo::MERGE_WARP;
-          const float* mm = reinterpret_cast<const float*>(area + 16 * Geo::MERGE_ROW * 4);
-          const float w = fast_exp2(mm[rr] - M);
-          L += mm[16 + rr] * w;
-          const float4 v = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(area) +
-                                                            rr * Geo::MERGE_ROW + d);
-          acc.x += v.x * w;
-          acc.y += v.y * w;
-          acc.z += v.z * w;
-          acc.w += v.w * w;
-        }
-      }
-      const float inv = (L > 0.f) ? 1.f / L : 0.f;
-      acc.x *= inv;
-      acc.y *= inv;
-      acc.z *= inv;
-      acc.w *= inv;
-      if (it.nsplit == 1) {
-        const int hh = r / it.nq, qi = it.q0 + r % it.nq;
-        __nv_bfloat16* dst = p.out + static_cast<int64_t>(row0 + qi) * p.o_st +
-                             static_cast<int64_t>(it.h * p.n_rep + hh) * p.o_sh + d;
-        uint2 pk;
-        pk.x = pack_bf16(acc.x, acc.y);
-        pk.y = pack_bf16(acc.z, acc.w);
-        *reinterpret_cast<uint2*>(dst) = pk;
-      } else {
-        float* po = p.p_o + (static_cast<int64_t>(blockIdx.x) * kMaxRows + r) * D + d;
-        *reinterpret_cast<float4*>(po) = acc;
-        if (d == 0) p.p_lse[static_cast<int64_t>(blockIdx.x) * kMaxRows + r] = (L > 0.f) ? M + fast_log2(L) : -INFINITY;
-      }
-    }
-  }
-
-  if (aborted && threadIdx.x == 0) {
-    // let the copies this CTA issued land before it retires (bounded)
-    const int issued = *reinterpret_cast<volatile int*>(&s_issued);
-    for (int li = max(0, issued - kStages); li < issued; ++li) {
-      (void)mbar_wait(&full_bar[li % kStages], (li / kStages) & 1);
-    }
-  }
-}
+#include "split_kernel.cuh"
 
 // ---------------------------------------------------------------- merge kernel
-// One CTA per (group, query row); 128 threads = 4 split lanes x 32 dim quads.
+// One CTA per (group, query row) of groups with more than one split; 256 threads =
+// 8 split lanes x 32 dim quads.  The split lse values are loaded in one pass and
+// turned into weights in shared memory, then every lane streams its splits'
+// partial rows with independent loads.
 template <int D>
-__global__ void __launch_bounds__(128) merge_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(256) merge_kernel(const AttnParams p) {
   const int gi = blockIdx.x;
   if (gi >= p.hdr->num_groups) return;
   const GroupInfo grp = p.groups[gi];
@@ -569,41 +256,51 @@ __global__ void __launch_bounds__(128) merge_kernel(const AttnParams p) {
   const int r = blockIdx.y;
   if (r >= R) return;
   constexpr int NQ = D / 4;
-  constexpr int NL = 128 / NQ;  // split lanes
-  const int dq = threadIdx.x % NQ, sl = threadIdx.x / NQ;
-  __shared__ float s_w[256];
-  __shared__ float s_M;
+  constexpr int NL = 256 / NQ;  // split lanes
+  constexpr int MAXW = 1024;
+  __shared__ float s_w[MAXW];
+  __shared__ float s_red[8];
   __shared__ float4 s_acc[NL][NQ];
   __shared__ float s_L[NL];
-  if (threadIdx.x == 0) {
-    float M = -INFINITY;
-    for (int s = 0; s < grp.nsplit; ++s)
-      M = fmaxf(M, p.p_lse[static_cast<int64_t>(grp.first_item + s) * kMaxRows + r]);
-    s_M = M;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ns = min(grp.nsplit, MAXW);
+  if (grp.nsplit > MAXW && tid == 0) raise_status(p.status, SPECDEC_STATUS_BAD_LENGTH);
+  float mx = -INFINITY;
+  for (int s = tid; s < ns; s += 256) {
+    const float l = p.p_lse[static_cast<int64_t>(grp.first_item + s) * kMaxRows + r];
+    s_w[s] = l;
+    mx = fmaxf(mx, l);
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) s_red[warp] = mx;
   __syncthreads();
-  const float M = s_M;
+  float M = s_red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) M = fmaxf(M, s_red[w]);
+  for (int s = tid; s < ns; s += 256) s_w[s] = (M == -INFINITY) ? 0.f : fast_exp2(s_w[s] - M);
+  __syncthreads();
+  const int dq = tid % NQ, sl = tid / NQ;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   float L = 0.f;
-  if (M != -INFINITY) {
-    for (int s = sl; s < grp.nsplit; s += NL) {
-      const int64_t idx = static_cast<int64_t>(grp.first_item + s) * kMaxRows + r;
-      const float w = fast_exp2(p.p_lse[idx] - M);
-      const float4 v = *reinterpret_cast<const float4*>(p.p_o + idx * D + dq * 4);
-      acc.x += v.x * w;
-      acc.y += v.y * w;
-      acc.z += v.z * w;
-      acc.w += v.w * w;
-      L += w;
-    }
+#pragma unroll 4
+  for (int s = sl; s < ns; s += NL) {
+    const float w = s_w[s];
+    const float4 v = *reinterpret_cast<const float4*>(
+        p.p_o + (static_cast<int64_t>(grp.first_item + s) * kMaxRows + r) * D + dq * 4);
+    acc.x += v.x * w;
+    acc.y += v.y * w;
+    acc.z += v.z * w;
+    acc.w += v.w * w;
+    L += w;
   }
-  (void)s_w;
   s_acc[sl][dq] = acc;
   if (dq == 0) s_L[sl] = L;
   __syncthreads();
   if (sl == 0) {
     float4 a = s_acc[0][dq];
     float Lt = s_L[0];
+#pragma unroll
     for (int k = 1; k < NL; ++k) {
       const float4 b = s_acc[k][dq];
       a.x += b.x;
@@ -741,9 +438,10 @@ static int ctas_per_sm() {
 static int q_tile_for(int n_rep) { return n_rep >= kMaxRows ? 1 : kMaxRows / n_rep; }
 
 static int target_items_for(int num_sms, int occ) {
-  // two waves of resident CTAs so ragged item lengths balance; occupancy is
-  // capped at 4 so the workspace size never depends on a device query
-  return num_sms * (occ < 1 ? 1 : (occ > 4 ? 4 : occ)) * 2;
+  // the plan makes at most ~4 waves of one-CTA-per-SM items (see plan_kernel);
+  // this bound sizes the workspace and never depends on a device query
+  (void)occ;
+  return num_sms * 4;
 }
 
 // Records a profiling event; under stream capture it becomes an external
@@ -775,7 +473,7 @@ static int run_attention(AttnParams p, const CUtensorMap& kmap, const CUtensorMa
   if (int rc = record_event(ev_end, stream)) return rc;
   const int rows_max = p.n_rep * (p.q_tile < p.max_q_len ? p.q_tile : p.max_q_len);
   dim3 mgrid(p.max_groups, rows_max < kMaxRows ? rows_max : kMaxRows);
-  merge_kernel<D><<<mgrid, 128, 0, stream>>>(p);
+  merge_kernel<D><<<mgrid, 256, 0, stream>>>(p);
   return after_launch("merge_kernel");
 }
 

@@ -86,6 +86,18 @@ def oracle_rows(q_rows, ks, vrefs, q_lens, eager=False):
 
 
 def assert_close_attention(got, ref, what=""):
+    """Elementwise bar against the fp32 formula (reference.attention_fp32)."""
     ok, max_err, excess = oatt.within_tolerance(got, ref, RTOL, ATOL)
     assert ok, f"{what}: max |err| {max_err:.3e}, worst excess over tolerance {excess:.3e}"
     return max_err
+
+
+def assert_close_eager(got, ref, what=""):
+    """Bar against the eager engine path (reference.attention), whose scores are rounded to
+    bf16 before the softmax: the reference's own bf16 check (sample_experiment.py:45-47),
+    max |err| <= 2e-2 or <= 2 % of the output magnitude."""
+    err = (got.float().cpu() - ref.float().cpu()).abs().max().item()
+    scale = ref.float().abs().max().item()
+    assert torch.isfinite(got.float()).all(), f"{what}: non-finite output"
+    assert err <= 2e-2 or err <= 0.02 * max(scale, 1e-6), f"{what}: max |err| {err:.3e} (scale {scale:.3e})"
+    return err

@@ -94,7 +94,16 @@ def test_accept_workspace_is_reusable_in_a_graph():
     torch.cuda.synchronize()
     assert torch.equal(g1, g2) and torch.equal(m1, m2)
     assert torch.equal(g1, logits.float().argmax(-1).view(B, 5).to(torch.int32))
-    assert not ws.any()  # every ticket was reset by its last user
+    # every ticket was reset by its last user: the ticket arrays (after the per-chunk
+    # partials, 256-byte aligned) are zero again
+    chunks = -(-V // 8192)
+    rows = B * 5
+    a256 = lambda x: -(-x // 256) * 256  # noqa: E731
+    rt = a256(a256(rows * chunks * 4) + rows * chunks * 4)
+    st = a256(rt + rows * 4)
+    assert not ws[rt:rt + rows * 4].any() and not ws[st:st + B * 4].any()
+    g3, m3, _ = ops.greedy_accept(logits, workspace=ws, **args)
+    assert torch.equal(g1, g3) and torch.equal(m1, m3)
 
 
 def test_device_trim_rule():

@@ -1,15 +1,17 @@
 """GPU parity of the attention kernels against the oracle and the reference's golden outputs.
 
-Tolerance (north star): |got - ref| <= 1e-2 + 2e-2 * |ref| elementwise for bf16 outputs,
-against both the eager reference (bf16 scores) and its fp32 formula; 1e-4 absolute for
-the fp32 contiguous op (sample_experiment.py:21)."""
+Tolerance: against the fp32 formula (reference.attention_fp32) every bf16 output element
+satisfies |got - ref| <= 1e-2 + 2e-2 * |ref| (north star); against the eager engine path
+(reference.attention, bf16-rounded scores) the reference's own bf16 check applies
+(max |err| <= 2e-2 or <= 2 % of the output magnitude, sample_experiment.py:45-47);
+the fp32 contiguous op is held to 1e-4 absolute (sample_experiment.py:21)."""
 
 from __future__ import annotations
 
 import pytest
 import torch
 
-from gpu_helpers import assert_close_attention, build_cache, oracle_rows
+from gpu_helpers import assert_close_attention, assert_close_eager, build_cache, oracle_rows
 from oracle import attention as oatt
 
 pytestmark = pytest.mark.gpu
@@ -29,7 +31,7 @@ def test_contiguous_attention_matches_golden(golden):
         if q.dtype == torch.float32:
             torch.testing.assert_close(got, case["fp32"], rtol=0, atol=1e-4, msg=name)
             continue
-        assert_close_attention(got, case["eager"], f"{name} vs eager")
+        assert_close_eager(got, case["eager"], f"{name} vs eager")
         assert_close_attention(got, case["fp32"], f"{name} vs fp32")
 
 
@@ -43,7 +45,7 @@ def test_contiguous_attention_shapes(S, T, H, KV, D):
     v = torch.randn(2, KV, T, D, generator=g).to(torch.bfloat16)
     got = ops.attention(q.cuda(), k.cuda(), v.cuda()).cpu()
     assert_close_attention(got, oatt.attention_fp32(q, k, v), f"S={S} T={T}")
-    assert_close_attention(got, oatt.eager_attention(q, k, v), f"S={S} T={T} eager")
+    assert_close_eager(got, oatt.eager_attention(q, k, v), f"S={S} T={T} eager")
 
 
 def _paged_case(lens, q_lens, H, KV, D, fp8, seed):
@@ -74,7 +76,7 @@ def test_paged_attention_draft_geometry(S):
 def test_paged_attention_matches_eager_reference_fp8():
     got, _, q, ks, vrefs = _paged_case([2048], [5], 12, 2, 128, True, seed=99)
     ref = oracle_rows(q, ks, vrefs, [5], eager=True)
-    assert_close_attention(got, ref, "fp8 vs eager")
+    assert_close_eager(got, ref, "fp8 vs eager")
 
 
 @pytest.mark.parametrize("fp8", [False, True])
