@@ -139,6 +139,27 @@ int specdec_ragged_plan(const SpecdecAttnArgs* args, specdec_stream_t stream);
 int specdec_paged_attention(const SpecdecAttnArgs* args, specdec_stream_t stream);
 
 /*
+ * specdec_paged_attention without a caller workspace.  This entry point has no
+ * counterpart in the reference.  It serves callers that cannot allocate device
+ * memory: a plugin host that owns all device memory and gives a plugin only its
+ * inputs, outputs and a stream, or an FFI binding with no CUDA allocator of its
+ * own.  It allocates nothing (no cudaMalloc, no allocating library call); its
+ * scratch (plan + split partials) is a 32 MiB array compiled into the library,
+ * held by every GPU that loads the library until the process exits.
+ *   - args->workspace, args->workspace_bytes and args->reuse_plan are ignored; the
+ *     plan is rebuilt on every call.
+ *   - A batch needing more than 32 MiB of scratch (see specdec_attn_workspace_bytes)
+ *     is rejected with SPECDEC_ERR_WORKSPACE before anything is launched.
+ *   - The first call on a device looks up the scratch's device address with that
+ *     device current; make that first call before any stream capture.
+ *   - All calls share the one scratch area, which keeps the previous call's
+ *     contents (nothing in it needs to start at zero).  Calls whose kernels
+ *     overlap on the GPU (different streams, or different host threads) race on
+ *     it: serialise them on one stream.
+ */
+int specdec_paged_attention_noalloc(const SpecdecAttnArgs* args, specdec_stream_t stream);
+
+/*
  * Append n_new[b] tokens per sequence at positions pos0[b] .. pos0[b]+n_new[b]-1.
  * K is copied (bf16); V is copied (bf16 pool) or quantised to E4M3 with one
  * scale per token and KV head: s = max|v| / 448 (s = 1 when the max is 0),

@@ -27,6 +27,8 @@
 
 #include <math.h>
 
+#include <mutex>
+
 #include "sd_common.cuh"
 #include "sd_internal.h"
 
@@ -611,6 +613,63 @@ extern "C" int specdec_ragged_plan(const SpecdecAttnArgs* args, specdec_stream_t
 
 extern "C" int specdec_paged_attention(const SpecdecAttnArgs* args, specdec_stream_t stream) {
   return paged_entry(args, reinterpret_cast<cudaStream_t>(stream), false);
+}
+
+// ---------------------------------------------------------------- no-allocation variant
+// Some callers cannot hand this library any scratch memory: a plugin host that
+// owns every byte of device memory and passes a plugin only its inputs, outputs
+// and a stream, or an FFI binding (cgo, JNI, a C caller) that has no CUDA
+// allocator and must not call cudaMalloc itself.  For them the paged attention
+// call can use a fixed scratch area compiled into this library instead of the
+// caller's workspace.  The area is a file-scope device array of
+// kStaticScratchBytes (32 MiB), so every GPU that loads the library keeps those
+// 32 MiB until the process exits.  Batches whose plan and split partials need
+// more than that are rejected with SPECDEC_ERR_WORKSPACE.
+constexpr size_t kStaticScratchBytes = size_t(32) << 20;
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+
+// Host code cannot use g_static_scratch's name as a device address (on the host it
+// is only a stand-in symbol).  The device address is looked up once per device,
+// with that device current, and cached.
+static int static_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(SPECDEC_ERR_CUDA, "no current CUDA device for the static scratch");
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(SPECDEC_ERR_CUDA, "cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(e));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return SPECDEC_OK;
+}
+
+extern "C" int specdec_paged_attention_noalloc(const SpecdecAttnArgs* args, specdec_stream_t stream) {
+  if (int rc = validate_paged(args)) return rc;
+  const int n_rep = args->batch.num_q_heads / args->kv.num_kv_heads;
+  const int qt = q_tile_for(n_rep);
+  const int max_qtiles = (args->batch.max_q_len + qt - 1) / qt;
+  const int sms = args->num_sms > 0 ? args->num_sms : device_sm_count();
+  const size_t need =
+      ws_layout(args->batch.num_seqs, args->kv.num_kv_heads, max_qtiles, args->kv.head_dim, target_items_for(sms, 0))
+          .total;
+  if (need > kStaticScratchBytes)
+    return fail(SPECDEC_ERR_WORKSPACE,
+                "this batch needs %zu bytes of scratch; the static scratch of the no-allocation entry point "
+                "holds %zu bytes (use specdec_paged_attention with a caller workspace)",
+                need, kStaticScratchBytes);
+  void* scratch = nullptr;
+  if (int rc = static_scratch(&scratch)) return rc;
+  SpecdecAttnArgs a = *args;
+  a.workspace = scratch;
+  a.workspace_bytes = kStaticScratchBytes;
+  a.reuse_plan = 0;  // the shared scratch may hold another call's plan: always rebuild it
+  return paged_entry(&a, reinterpret_cast<cudaStream_t>(stream), false);
 }
 
 extern "C" size_t specdec_attention_workspace_bytes(int32_t B, int32_t H, int32_t KV, int32_t S, int32_t D,

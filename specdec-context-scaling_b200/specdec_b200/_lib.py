@@ -146,6 +146,7 @@ SIGNATURES = {
     "specdec_attn_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32, _i32, _i32]),
     "specdec_ragged_plan": (ctypes.c_int, [ctypes.POINTER(AttnArgs), _vp]),
     "specdec_paged_attention": (ctypes.c_int, [ctypes.POINTER(AttnArgs), _vp]),
+    "specdec_paged_attention_noalloc": (ctypes.c_int, [ctypes.POINTER(AttnArgs), _vp]),
     "specdec_append_kv": (ctypes.c_int, [ctypes.POINTER(AppendArgs), _vp]),
     "specdec_accept_workspace_bytes": (_sz, [_i32, _i32, _i32]),
     "specdec_greedy_accept": (ctypes.c_int, [ctypes.POINTER(AcceptArgs), _vp]),
