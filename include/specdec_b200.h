@@ -255,6 +255,12 @@ int specdec_swiglu(const void* gate, const void* up, void* out, int32_t dtype, i
                    specdec_stream_t stream);
 
 /* Diagnostics. */
+/* Tensor-core self-check (no counterpart in the reference): one CTA computes, with
+   tcgen05 MMAs from 128-byte-swizzled shared memory into TMEM,
+   out1[128][32] = k[128][128] . q[32][128]^T and out2[128][32] = v[128][128]^T . p[32][128]^T
+   (bf16 row-major inputs, fp32 outputs) -- the operand layouts of the verify kernel. */
+int specdec_umma_selftest(const void* k, const void* q, const void* v, const void* p, float* out1, float* out2,
+                          int32_t* status, specdec_stream_t stream);
 const char* specdec_last_error(void);
 int specdec_abi_version(void);
 /* Number of kernels this library launched since load (all entry points). */
