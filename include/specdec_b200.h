@@ -67,8 +67,8 @@ typedef enum SpecdecDtype { SPECDEC_F32 = 0, SPECDEC_BF16 = 1, SPECDEC_E4M3 = 2 
  *            block in the 128-byte-swizzled order that a TMA SWIZZLE_128B
  *            load of a {64 dims x 16 tokens} box writes to shared memory.
  *   v_pool : bf16 in the k_pool order            (v_dtype == SPECDEC_BF16), or
- *            e4m3 [num_pages][num_kv_heads][head_dim][16] with the 16 token
- *            bytes of a dim in MMA-fragment order (v_dtype == SPECDEC_E4M3).
+ *            e4m3 [num_pages][num_kv_heads][16][head_dim] code rows
+ *            (v_dtype == SPECDEC_E4M3).
  *   v_scale: f32 [num_pages][num_kv_heads][16]: one max-abs/448 scale per
  *            token and KV head (E4M3 only; NULL for bf16 V).
  *   page_table: int32 [num_seqs][max_pages_per_seq]; token t of sequence b

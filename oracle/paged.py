@@ -10,7 +10,7 @@ so appends, trims and attention can be checked bit-exactly.
 
 Block layouts (per page, per KV head):
   bf16 K / V : element (r, d) at  (d // 64) * 1024 + r * 64 + (((d % 64) // 8) ^ (r % 8)) * 8 + d % 8
-  E4M3 V     : byte    (r, d) at  d * 16 + vpos(r),  vpos(r) = 4 * ((r % 8) // 2) + 2 * (r // 8) + r % 2
+  E4M3 V     : byte    (r, d) at  r * D + d  (plain token rows)
   scales     : (r) at r
 """
 
@@ -19,10 +19,6 @@ from __future__ import annotations
 import numpy as np
 
 PAGE = 16
-
-
-def vpos(r: int) -> int:
-    return 4 * ((r % 8) // 2) + 2 * (r // 8) + (r % 2)
 
 
 def kblock_perm(head_dim: int) -> np.ndarray:
@@ -35,11 +31,7 @@ def kblock_perm(head_dim: int) -> np.ndarray:
 
 
 def vblock_perm(head_dim: int) -> np.ndarray:
-    out = np.empty(PAGE * head_dim, dtype=np.int64)
-    for r in range(PAGE):
-        for d in range(head_dim):
-            out[r * head_dim + d] = d * PAGE + vpos(r)
-    return out
+    return np.arange(PAGE * head_dim, dtype=np.int64)
 
 
 def random_page_table(num_seqs: int, max_pages: int, num_pages: int, seed: int) -> np.ndarray:

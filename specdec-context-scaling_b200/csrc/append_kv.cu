@@ -12,7 +12,7 @@
 //
 // One warp per (sequence, new token, KV head); lanes own 4 (D=128) or 2 (D=64)
 // consecutive dims.  The K row and a bf16 V row go to the swizzled page-block
-// order; E4M3 codes go to the [dim][16] fragment order (see sd_common.cuh).
+// order; E4M3 codes go to plain [16 tokens][D] rows of the page block.
 #include "sd_common.cuh"
 #include "sd_internal.h"
 
@@ -101,14 +101,15 @@ __global__ void __launch_bounds__(256) append_kernel(const AppendParams p) {
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float s = __fdiv_rn(m, kE4M3Max);
     if (s == 0.f) s = 1.f;
-    uint8_t* vblk = p.v_pool + ph * (D * 16);
-    const int vp = vpos(slot);
+    // natural [16 tokens][D] code rows: each lane writes its 4 codes as one word
+    uint8_t* vrow = p.v_pool + ph * (D * 16) + slot * D;
+    uint32_t word = 0;
 #pragma unroll
     for (int e = 0; e < PER; e += 2) {
       const uint32_t two = f32x2_to_e4m3x2(__fdiv_rn(x[e], s), __fdiv_rn(x[e + 1], s));
-      vblk[(d0 + e) * 16 + vp] = static_cast<uint8_t>(two & 0xFFu);
-      vblk[(d0 + e + 1) * 16 + vp] = static_cast<uint8_t>(two >> 8);
+      word |= two << (8 * e);
     }
+    *reinterpret_cast<uint32_t*>(vrow + d0) = word;
     if (lane == 0) p.v_scale[ph * kPage + slot] = s;
   }
 }

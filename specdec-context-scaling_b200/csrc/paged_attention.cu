@@ -31,6 +31,7 @@
 
 #include "sd_common.cuh"
 #include "sd_internal.h"
+#include "umma.cuh"
 
 namespace sd {
 
@@ -89,6 +90,7 @@ struct AttnParams {
   float* p_lse;
   float* p_o;
   int32_t max_items, max_groups, target_items;
+  int32_t tile_pages;  // the split kernel consumes keys in tiles of this many pages
   int32_t* status;
 };
 
@@ -180,6 +182,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
     pps = max(pps, 64);
   }
   pps = max(pps, 1);
+  if (pps > p.tile_pages) pps = (pps + p.tile_pages - 1) / p.tile_pages * p.tile_pages;
 
   int carry = 0;
   for (int base = 0; base < ngroups; base += blockDim.x) {
@@ -242,6 +245,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
 
 // ---------------------------------------------------------------- split kernel
 #include "split_kernel.cuh"
+#include "verify_kernel.cuh"
 
 // ---------------------------------------------------------------- merge kernel
 // One CTA per (group, query row) of groups with more than one split; 256 threads =
@@ -423,21 +427,42 @@ static int encode_kv_map(CUtensorMap* map, const void* base, int planes, int T, 
   return SPECDEC_OK;
 }
 
-template <int D, bool VF8, bool TMAP>
-static int ctas_per_sm() {
-  static int cached = 0;
-  if (cached == 0) {
-    using Geo = StageGeom<D, VF8>;
-    auto kern = split_kernel<D, VF8, TMAP>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo::SMEM);
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, Geo::SMEM) != cudaSuccess || n <= 0) n = 1;
-    cached = n;
+// Query positions per work item: rows (n_rep x positions) must fit the split
+// kernel's row tile -- 32 rows for the tcgen05 kernel (head_dim 128), 64 otherwise.
+static int q_tile_for(int n_rep, int D) {
+  const int rows = (D == 128) ? 32 : kMaxRows;
+  return n_rep >= rows ? 1 : rows / n_rep;
+}
+static int tile_pages_for(int D) { return D == 128 ? kTilePages : 1; }
+
+// dynamic shared memory opt-in, once per (kernel, device)
+template <typename K>
+static void set_smem_attr(K kern, int bytes, bool* done_per_device) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  if (!done_per_device[dev]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    done_per_device[dev] = true;
   }
-  return cached;
 }
 
-static int q_tile_for(int n_rep) { return n_rep >= kMaxRows ? 1 : kMaxRows / n_rep; }
+template <int NR, bool VF8, bool TMAP>
+static int launch_verify(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, cudaStream_t st) {
+  using Geo = V3Geom<NR, VF8>;
+  static bool attr[64] = {};
+  set_smem_attr(verify_kernel<NR, VF8, TMAP>, Geo::SMEM, attr);
+  verify_kernel<NR, VF8, TMAP><<<p.max_items, kV3Threads, Geo::SMEM, st>>>(p, kmap, vmap);
+  return after_launch("verify_kernel");
+}
+
+template <bool TMAP>
+static int launch_split64(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, cudaStream_t st) {
+  using Geo = StageGeom<64, false>;
+  static bool attr[64] = {};
+  set_smem_attr(split_kernel<64, false, TMAP>, Geo::SMEM, attr);
+  split_kernel<64, false, TMAP><<<p.max_items, kThreads, Geo::SMEM, st>>>(p, kmap, vmap);
+  return after_launch("split_kernel");
+}
 
 static int target_items_for(int num_sms, int occ) {
   // the plan makes at most ~4 waves of one-CTA-per-SM items (see plan_kernel);
@@ -462,17 +487,21 @@ static int record_event(void* ev, cudaStream_t stream) {
 template <int D, bool VF8, bool TMAP>
 static int run_attention(AttnParams p, const CUtensorMap& kmap, const CUtensorMap& vmap, bool build_plan,
                          cudaStream_t stream, void* ev_begin = nullptr, void* ev_end = nullptr) {
-  using Geo = StageGeom<D, VF8>;
   if (build_plan) {
     plan_kernel<<<1, 1024, 0, stream>>>(p);
     if (int rc = after_launch("plan_kernel")) return rc;
   }
-  auto kern = split_kernel<D, VF8, TMAP>;
-  (void)ctas_per_sm<D, VF8, TMAP>();  // sets the dynamic smem attribute once
   if (int rc = record_event(ev_begin, stream)) return rc;
-  kern<<<p.max_items, kThreads, Geo::SMEM, stream>>>(p, kmap, vmap);
-  if (int rc = after_launch("split_kernel")) return rc;
-  if (int rc = record_event(ev_end, stream)) return rc;
+  int rc = SPECDEC_OK;
+  if constexpr (D == 128) {
+    const int rows_max = p.n_rep * (p.q_tile < p.max_q_len ? p.q_tile : p.max_q_len);
+    rc = rows_max <= 16 ? launch_verify<16, VF8, TMAP>(p, kmap, vmap, stream)
+                        : launch_verify<32, VF8, TMAP>(p, kmap, vmap, stream);
+  } else {
+    rc = launch_split64<TMAP>(p, kmap, vmap, stream);
+  }
+  if (rc) return rc;
+  if (int rc2 = record_event(ev_end, stream)) return rc2;
   const int rows_max = p.n_rep * (p.q_tile < p.max_q_len ? p.q_tile : p.max_q_len);
   dim3 mgrid(p.max_groups, rows_max < kMaxRows ? rows_max : kMaxRows);
   merge_kernel<D><<<mgrid, 256, 0, stream>>>(p);
@@ -499,11 +528,10 @@ static int fill_workspace(AttnParams& p, void* ws, size_t ws_bytes, int B, int K
 }
 
 static int occupancy_for(int D, bool vf8, bool tmap) {
-  if (D == 128) {
-    if (tmap) return ctas_per_sm<128, false, true>();
-    return vf8 ? ctas_per_sm<128, true, false>() : ctas_per_sm<128, false, false>();
-  }
-  return tmap ? ctas_per_sm<64, false, true>() : ctas_per_sm<64, false, false>();
+  (void)D;
+  (void)vf8;
+  (void)tmap;
+  return 1;  // both split kernels run one CTA per SM
 }
 
 static int validate_paged(const SpecdecAttnArgs* a) {
@@ -516,8 +544,8 @@ static int validate_paged(const SpecdecAttnArgs* a) {
   if (bt.num_seqs <= 0 || bt.num_q_heads <= 0 || kv.num_kv_heads <= 0)
     return fail(SPECDEC_ERR_INVALID, "num_seqs, num_q_heads and num_kv_heads must be positive");
   if (bt.num_q_heads % kv.num_kv_heads != 0) return fail(SPECDEC_ERR_INVALID, "query heads must divide KV heads");
-  if (bt.num_q_heads / kv.num_kv_heads > kMaxRows)
-    return fail(SPECDEC_ERR_UNSUPPORTED, "more than %d query heads per KV head", kMaxRows);
+  if (bt.num_q_heads / kv.num_kv_heads > (kv.head_dim == 128 ? 32 : kMaxRows))
+    return fail(SPECDEC_ERR_UNSUPPORTED, "too many query heads per KV head (32 for head_dim 128, %d for 64)", kMaxRows);
   if (kv.head_dim != 64 && kv.head_dim != 128) return fail(SPECDEC_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
   if (kv.v_dtype != SPECDEC_BF16 && kv.v_dtype != SPECDEC_E4M3)
     return fail(SPECDEC_ERR_UNSUPPORTED, "v_dtype must be SPECDEC_BF16 or SPECDEC_E4M3");
@@ -553,7 +581,8 @@ static AttnParams params_from(const SpecdecAttnArgs* a) {
   p.KV = a->kv.num_kv_heads;
   p.n_rep = p.H / p.KV;
   p.max_q_len = a->batch.max_q_len;
-  p.q_tile = q_tile_for(p.n_rep);
+  p.q_tile = q_tile_for(p.n_rep, a->kv.head_dim);
+  p.tile_pages = tile_pages_for(a->kv.head_dim);
   p.max_qtiles = (p.max_q_len + p.q_tile - 1) / p.q_tile;
   p.k_pool = static_cast<const uint8_t*>(a->kv.k_pool);
   p.v_pool = static_cast<const uint8_t*>(a->kv.v_pool);
@@ -599,7 +628,7 @@ extern "C" size_t specdec_attn_workspace_bytes(int32_t num_seqs, int32_t num_q_h
   if (num_seqs <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || max_q_len <= 0 || num_q_heads % num_kv_heads)
     return 0;
   const int n_rep = num_q_heads / num_kv_heads;
-  const int qt = q_tile_for(n_rep);
+  const int qt = q_tile_for(n_rep, head_dim);
   const int max_qtiles = (max_q_len + qt - 1) / qt;
   const int sms = num_sms > 0 ? num_sms : device_sm_count();
   // occupancy is not known without a device query; size for 4 CTAs per SM (an upper bound)
@@ -652,7 +681,7 @@ static int static_scratch(void** out) {
 extern "C" int specdec_paged_attention_noalloc(const SpecdecAttnArgs* args, specdec_stream_t stream) {
   if (int rc = validate_paged(args)) return rc;
   const int n_rep = args->batch.num_q_heads / args->kv.num_kv_heads;
-  const int qt = q_tile_for(n_rep);
+  const int qt = q_tile_for(n_rep, args->kv.head_dim);
   const int max_qtiles = (args->batch.max_q_len + qt - 1) / qt;
   const int sms = args->num_sms > 0 ? args->num_sms : device_sm_count();
   const size_t need =
@@ -716,8 +745,10 @@ extern "C" int specdec_attention(const void* q, const void* k, const void* v, vo
   p.KV = KV;
   p.n_rep = H / KV;
   if (p.n_rep > kMaxRows) return fail(SPECDEC_ERR_UNSUPPORTED, "more than %d query heads per KV head", kMaxRows);
+  if (D == 128 && p.n_rep > 32) return fail(SPECDEC_ERR_UNSUPPORTED, "head_dim 128 supports at most 32 query heads per KV head");
   p.max_q_len = S;
-  p.q_tile = q_tile_for(p.n_rep);
+  p.q_tile = q_tile_for(p.n_rep, D);
+  p.tile_pages = tile_pages_for(D);
   p.max_qtiles = (S + p.q_tile - 1) / p.q_tile;
   p.num_pages = 1;
   p.max_pages = (T + kPage - 1) / kPage;

@@ -72,7 +72,7 @@ SD_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
-// ---------------------------------------------------------------- bulk TMA (no multicast anywhere)
+// ---------------------------------------------------------------- bulk TMA (plain per-CTA loads)
 // 1-D bulk copy global -> shared, completion counted on `bar` in bytes.
 // src/dst 16-byte aligned, bytes a multiple of 16.
 SD_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -178,9 +178,6 @@ SD_DEV uint32_t kblock_offset(int r, int d) {
 SD_DEV uint32_t kblock_chunk_offset(int r, int c) {
   return static_cast<uint32_t>((c >> 3) * 2048 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
-// E4M3 V page-head block: [D dims][16 bytes]; token r of dim d is byte
-// d * 16 + vpos(r), where vpos places tokens (2c, 2c+1, 2c+8, 2c+9) in bytes
-// 4c .. 4c+3 so a 32-bit load is the two halves of an m16n8k16 B fragment.
-SD_DEV int vpos(int r) { return (((r & 7) >> 1) << 2) + ((r >> 3) << 1) + (r & 1); }
+// E4M3 V page-head block: plain [16 tokens][D] code rows (token r, dim d at r * D + d).
 
 }  // namespace sd

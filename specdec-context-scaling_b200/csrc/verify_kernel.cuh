@@ -1,0 +1,97 @@
+// verify_kernel.cuh -- split-KV decode / verify attention on the fifth-generation
+// tensor cores (tcgen05, TMEM accumulators) for head_dim 128.  Included inside
+// namespace sd by paged_attention.cu, after split_kernel.cuh.
+//
+// One CTA per work item (sequence b, KV head h, key range), 192 threads:
+//   warps 0-3  softmax + epilogue; thread t owns key t of each 128-key tile (TMEM
+//              lane t) and, in the epilogue, output dim t
+//   warp 4     producer: bulk-TMA copies of the item's pages into an NS-deep ring of
+//              128-key tiles (K [2 halves][128 rows][128 B] in the 128-byte-swizzled
+//              image of the pool; V likewise, or raw E4M3 rows + per-token scales)
+//   warp 5     MMA issuer (one lane) and owner of the TMEM allocation
+// Per tile t (buffer b = t & 1):
+//   S^T[b] (128 keys x NR rows, fp32, TMEM)  = K_tile . Q^T            (8 x K=16 MMAs)
+//   softmax warps: row maxima over the tile, lazy online rescale of O (only when a
+//   row max grows by more than 2^8), P = exp2(S - M) written to shared memory as
+//   the K-major B operand; E4M3 tiles are widened to f16 in shared memory and the
+//   per-token scale is folded into P
+//   O^T (128 dims x NR rows, fp32, TMEM)    += V_tile^T . P^T           (8 MMAs)
+// QK^T of tile t+1 is issued before PV of tile t, so softmax and MMAs overlap.
+// Rows: the n_rep query heads x q query positions of one KV head (NR = 16 or 32).
+#pragma once
+
+constexpr int kV3Threads = 192;
+constexpr int kTileKeys = 128;
+constexpr int kTilePages = 8;
+constexpr float kRescaleLog2 = 8.f;   // lazy rescale threshold (log2 units)
+constexpr float kScaleSlack = 16.f;   // lazy growth of the E4M3 reference scale
+
+template <int NR, bool VF8>
+struct V3Geom {
+  static constexpr int NS = VF8 ? 2 : 3;                 // ring depth (tiles)
+  static constexpr int KT = 32768;                       // K tile bytes
+  static constexpr int VT = VF8 ? 16384 : 32768;         // V tile bytes as staged
+  static constexpr int ST = VF8 ? 512 : 0;               // 128 scales
+  static constexpr int K_OFF = 0;
+  static constexpr int V_OFF = K_OFF + NS * KT;
+  static constexpr int S_OFF = V_OFF + NS * VT;
+  static constexpr int VC_OFF = ((S_OFF + NS * ST + 1023) / 1024) * 1024;  // widened V (E4M3 only)
+  static constexpr int Q_OFF = VC_OFF + (VF8 ? 2 * 32768 : 0);
+  static constexpr int QB = NR * 256;                    // [2 halves][NR rows][128 B]
+  static constexpr int P_OFF = Q_OFF + QB;
+  static constexpr int SMEM = P_OFF + 2 * QB + 1024;     // + alignment slack
+  static constexpr int TMEM_COLS = NR <= 16 ? 64 : 128;  // S[2] + O = 3 NR columns
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+};
+
+// Row-wise maximum / sum over the 32 keys of a warp when each lane holds one key's
+// NR row values: a transposing butterfly -- at each step a lane keeps one half of
+// its values and swaps the other half with its partner.  Afterwards lane l holds
+// the result for row (l % NR).
+template <int NR>
+SD_DEV float warp_rows_max(const float (&v)[NR], int lane) {
+  float a[NR];
+#pragma unroll
+  for (int i = 0; i < NR; ++i) a[i] = v[i];
+#pragma unroll
+  for (int off = NR / 2; off >= 1; off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < off; ++i) {
+      const float send = upper ? a[i] : a[i + off];
+      const float keep = upper ? a[i + off] : a[i];
+      a[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, off));
+    }
+  }
+  if (NR < 32) {
+#pragma unroll
+    for (int off = NR; off < 32; off <<= 1) a[0] = fmaxf(a[0], __shfl_xor_sync(0xffffffffu, a[0], off));
+  }
+  return a[0];
+}
+template <int NR>
+SD_DEV float warp_rows_sum(const float (&v)[NR], int lane) {
+  float a[NR];
+#pragma unroll
+  for (int i = 0; i < NR; ++i) a[i] = v[i];
+#pragma unroll
+  for (int off = NR / 2; off >= 1; off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < off; ++i) {
+      const float send = upper ? a[i] : a[i + off];
+      const float keep = upper ? a[i + off] : a[i];
+      a[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  if (NR < 32) {
+#pragma unroll
+    for (int off = NR; off < 32; off <<= 1) a[0] += __shfl_xor_sync(0xffffffffu, a[0], off);
+  }
+  return a[0];
+}
+
+// warp-uniform bounded wait; returns false when any lane gave up
+SD_DEV bool warp_wait(uint64_t* bar, uint32_t parity) { return __all_sync(0xffffffffu, mbar_wait(bar, parity)); }
+
+#include "verify_kernel_body.inc"

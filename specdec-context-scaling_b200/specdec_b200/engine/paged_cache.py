@@ -7,9 +7,9 @@ into shared memory with one bulk-TMA copy):
   half-tiles of [16 rows][128 bytes]; 16-byte chunk ``j`` of row ``r`` is stored
   at chunk position ``j ^ (r & 7)`` -- the image a TMA SWIZZLE_128B load of a
   {64, 16} box writes to shared memory.
-* V as E4M3: [head_dim][16] bytes; token ``r`` of dim ``d`` is byte
-  ``d * 16 + vpos(r)`` with ``vpos`` placing tokens (2c, 2c+1, 2c+8, 2c+9) in
-  bytes 4c..4c+3 (one 32-bit shared load = one MMA B fragment).
+* V as E4M3: plain [16 tokens][head_dim] code rows (token ``r``, dim ``d`` at
+  byte ``r * head_dim + d``); the verify kernel widens a tile to f16 in shared
+  memory before its PV MMA.
 * V scales: [16] fp32 per (page, kv head).
 
 The reference cache (specdec/engine/model_self.py:778-800, contract in
@@ -30,13 +30,6 @@ import torch
 PAGE = 16
 
 
-def _vpos_table() -> list[int]:
-    return [(((r & 7) >> 1) << 2) + ((r >> 3) << 1) + (r & 1) for r in range(PAGE)]
-
-
-VPOS = _vpos_table()
-
-
 def kblock_index(head_dim: int, device=None) -> torch.Tensor:
     """Element permutation of a bf16 page-head block: ``block.flatten()[idx] = rows.flatten()``.
 
@@ -50,11 +43,8 @@ def kblock_index(head_dim: int, device=None) -> torch.Tensor:
 
 
 def vblock_index(head_dim: int, device=None) -> torch.Tensor:
-    """Byte permutation of an E4M3 page-head block: ``idx[r * head_dim + d] = d * 16 + vpos(r)``."""
-    r = torch.arange(PAGE, device=device).view(PAGE, 1)
-    d = torch.arange(head_dim, device=device).view(1, head_dim)
-    vp = torch.tensor(VPOS, device=device).view(PAGE, 1)
-    return (d * PAGE + vp).reshape(-1)
+    """Byte offsets of an E4M3 page-head block: ``idx[r * head_dim + d] = r * head_dim + d`` (plain rows)."""
+    return torch.arange(PAGE * head_dim, device=device)
 
 
 @dataclass
