@@ -28,6 +28,7 @@
 #include <math.h>
 
 #include <mutex>
+#include <utility>
 
 #include "sd_common.cuh"
 #include "sd_internal.h"
@@ -36,11 +37,14 @@
 namespace sd {
 
 // ---------------------------------------------------------------- plan records
-struct WorkItem {             // 32 bytes
+struct WorkItem {             // 48 bytes
   int32_t b, h, q0, nq;       // sequence, kv head, first query row, query rows in the tile
   int32_t page_begin, page_end;  // key blocks [page_begin, page_end) of 16 tokens
   int32_t group, nsplit;      // merge group; splits in the group (1 = write the output directly)
+  int32_t ctx, qlen, row0;    // the sequence's context length, query rows and first output row
+  int32_t cta;                // the persistent CTA that processes the item
 };
+static_assert(sizeof(WorkItem) == 48, "work item is 48 bytes");
 struct GroupInfo {
   int32_t first_item, nsplit, b, h, q0, nq, pad0, pad1;
 };
@@ -53,7 +57,7 @@ static_assert(sizeof(PlanHeader) == 256, "plan header is 256 bytes");
 constexpr int kMaxRows = 64;  // query rows (n_rep x query positions) per work item
 
 struct WsLayout {
-  size_t items, groups, lse, po, total;
+  size_t items, groups, ctas, lse, po, total;
   int32_t max_items, max_groups;
 };
 
@@ -63,7 +67,8 @@ static WsLayout ws_layout(int B, int KV, int max_qtiles, int D, int target_items
   w.max_items = target_items + w.max_groups;
   w.items = sizeof(PlanHeader);
   w.groups = align_up(w.items + sizeof(WorkItem) * (size_t)w.max_items, 256);
-  w.lse = align_up(w.groups + sizeof(GroupInfo) * (size_t)w.max_groups, 256);
+  w.ctas = align_up(w.groups + sizeof(GroupInfo) * (size_t)w.max_groups, 256);
+  w.lse = align_up(w.ctas + sizeof(int32_t) * (size_t)(target_items / 4 + 1), 256);
   w.po = align_up(w.lse + sizeof(float) * kMaxRows * (size_t)w.max_items, 256);
   w.total = align_up(w.po + sizeof(float) * kMaxRows * (size_t)D * w.max_items, 256);
   return w;
@@ -87,6 +92,7 @@ struct AttnParams {
   PlanHeader* hdr;
   WorkItem* items;
   GroupInfo* groups;
+  int32_t* cta_first;  // [C + 1]: items of persistent CTA c are cta_first[c] .. cta_first[c+1]-1
   float* p_lse;
   float* p_o;
   int32_t max_items, max_groups, target_items;
@@ -156,7 +162,8 @@ SD_DEV int block_exclusive_scan(int v, int& total, int* s_warp) {
 __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
   __shared__ int s_warp[32];
   __shared__ long long s_total;
-  __shared__ int s_first[1024], s_pages[1024], s_nq[1024];
+  __shared__ int s_first[1024], s_pages[1024], s_nq[1024], s_c0[1024];
+  __shared__ long long s_start[1024];
   const int ngroups = p.max_groups;
   if (threadIdx.x == 0) s_total = 0;
   __syncthreads();
@@ -171,25 +178,30 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
   if ((threadIdx.x & 31) == 0) atomicAdd(reinterpret_cast<unsigned long long*>(&s_total),
                                          static_cast<unsigned long long>(local));
   __syncthreads();
-  const long long total = s_total;
-  // pages per split: one wave of CTAs (one per SM) while that keeps a CTA at <= 64
-  // pages; above that ~4 waves of >= 64-page items so ragged lengths balance.
-  // Either way num_items <= total / pps + groups <= 4 * num_sms + groups = max_items.
-  const int sms = p.target_items / 4;
-  int pps = static_cast<int>((total + sms - 1) / sms);
-  if (pps > 64) {
-    pps = static_cast<int>((total + 4LL * sms - 1) / (4LL * sms));
-    pps = max(pps, 64);
-  }
-  pps = max(pps, 1);
-  if (pps > p.tile_pages) pps = (pps + p.tile_pages - 1) / p.tile_pages * p.tile_pages;
+  const long long P = s_total;
+  // Balanced split: the concatenation of every group's pages (groups in order) is
+  // cut into C equal ranges, range c = [c*P/C, (c+1)*P/C) for CTA c of the
+  // persistent kernel.  An item is the intersection of a range with a group, so
+  // a group yields one item per range it meets: num_items <= C + groups.
+  // C <= P keeps every range non-empty (so no item is empty); the CTAs past C get no items
+  const int grid = p.target_items / 4;
+  const int C = static_cast<int>(min(static_cast<long long>(grid), max(P, 1LL)));
+  auto cta_of = [&](long long pos) { return static_cast<int>(((pos + 1) * C + P - 1) / P) - 1; };
+  auto range_lo = [&](int c) { return static_cast<long long>(c) * P / C; };
 
   int carry = 0;
+  long long pcarry = 0;
   for (int base = 0; base < ngroups; base += blockDim.x) {
     const int gi = base + threadIdx.x;
     int b = 0, h = 0, q0 = 0, nq = 0, pages = 0;
     if (gi < ngroups) pages = group_pages(p, gi, b, h, q0, nq);
-    const int n = (pages + pps - 1) / pps;
+    int chunk_pages;
+    const long long start = pcarry + block_exclusive_scan(pages, chunk_pages, s_warp);
+    int n = 0, c0 = 0;
+    if (pages > 0) {
+      c0 = cta_of(start);
+      n = cta_of(start + pages - 1) - c0 + 1;
+    }
     int chunk_total;
     const int first = carry + block_exclusive_scan(n, chunk_total, s_warp);
     if (gi < ngroups) {
@@ -208,6 +220,8 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
     s_first[threadIdx.x] = (gi < ngroups) ? first - carry : 0x7fffffff;
     s_pages[threadIdx.x] = pages;
     s_nq[threadIdx.x] = nq;
+    s_c0[threadIdx.x] = c0;
+    s_start[threadIdx.x] = start;
     __syncthreads();
     for (int i = threadIdx.x; i < chunk_total; i += blockDim.x) {
       int lo = 0, hi = blockDim.x - 1;
@@ -216,7 +230,8 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
         if (s_first[mid] <= i) lo = mid; else hi = mid - 1;
       }
       const int g2 = base + lo;
-      const int s = i - s_first[lo];
+      const int c = s_c0[lo] + (i - s_first[lo]);
+      const long long gs = s_start[lo];
       const int pg = s_pages[lo];
       const int per_b = p.max_qtiles * p.KV;
       const int b2 = g2 / per_b;
@@ -226,24 +241,37 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
       it.h = rem % p.KV;
       it.q0 = (rem / p.KV) * p.q_tile;
       it.nq = s_nq[lo];
-      it.page_begin = s * pps;
-      it.page_end = min((s + 1) * pps, pg);
+      it.page_begin = static_cast<int>(max(range_lo(c) - gs, 0LL));
+      it.page_end = static_cast<int>(min(range_lo(c + 1) - gs, static_cast<long long>(pg)));
       it.group = g2;
-      it.nsplit = (pg + pps - 1) / pps;
+      it.nsplit = cta_of(gs + pg - 1) - s_c0[lo] + 1;
+      it.ctx = seq_ctx_len(p, b2);
+      it.qlen = seq_q_len(p, b2);
+      it.row0 = seq_row0(p, b2);
+      it.cta = c;
       p.items[carry + i] = it;
     }
     __syncthreads();
     carry += chunk_total;
+    pcarry += chunk_pages;
+  }
+  // first item of every CTA of the grid (items are ordered by CTA): cta_first[c] .. cta_first[c+1]
+  for (int c = threadIdx.x; c <= grid; c += blockDim.x) {
+    int lo = 0, hi = carry;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (p.items[mid].cta < c) lo = mid + 1; else hi = mid;
+    }
+    p.cta_first[c] = lo;
   }
   if (threadIdx.x == 0) {
     p.hdr->num_items = carry;
-    p.hdr->pages_per_split = pps;
+    p.hdr->pages_per_split = static_cast<int32_t>(C > 0 ? (P + C - 1) / C : 0);
     p.hdr->num_groups = ngroups;
-    p.hdr->total_pages = static_cast<int32_t>(total);
+    p.hdr->total_pages = static_cast<int32_t>(P);
   }
 }
 
-// ---------------------------------------------------------------- split kernel
 #include "split_kernel.cuh"
 #include "verify_kernel.cuh"
 
@@ -254,6 +282,8 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
 // partial rows with independent loads.
 template <int D>
 __global__ void __launch_bounds__(256) merge_kernel(const AttnParams p) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int gi = blockIdx.x;
   if (gi >= p.hdr->num_groups) return;
   const GroupInfo grp = p.groups[gi];
@@ -446,22 +476,48 @@ static void set_smem_attr(K kern, int bytes, bool* done_per_device) {
   }
 }
 
+// Launches with programmatic stream serialization when `pdl` is set: the kernel may
+// start (and run the part before its grid_dep_wait) while the previous kernel on the
+// stream finishes.  Kernels launched this way read and write device data only after
+// grid_dep_wait().
+template <typename... KArgs, typename... Args>
+static int launch_k(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                    bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e != cudaSuccess) return fail(SPECDEC_ERR_CUDA, "%s launch: %s", what, cudaGetErrorString(e));
+  return after_launch(what);
+}
+
 template <int NR, bool VF8, bool TMAP>
-static int launch_verify(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, cudaStream_t st) {
+static int launch_verify(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, cudaStream_t st,
+                         bool pdl) {
   using Geo = V3Geom<NR, VF8>;
   static bool attr[64] = {};
   set_smem_attr(verify_kernel<NR, VF8, TMAP>, Geo::SMEM, attr);
-  verify_kernel<NR, VF8, TMAP><<<p.max_items, kV3Threads, Geo::SMEM, st>>>(p, kmap, vmap);
-  return after_launch("verify_kernel");
+  // persistent: one CTA per SM, the plan's C = target_items / 4 ranges
+  const int grid = p.target_items / 4;
+  return launch_k("verify_kernel", verify_kernel<NR, VF8, TMAP>, dim3(grid), dim3(kV3Threads), Geo::SMEM, st,
+                  pdl, p, kmap, vmap);
 }
 
 template <bool TMAP>
-static int launch_split64(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, cudaStream_t st) {
+static int launch_split64(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, cudaStream_t st,
+                          bool pdl) {
   using Geo = StageGeom<64, false>;
   static bool attr[64] = {};
   set_smem_attr(split_kernel<64, false, TMAP>, Geo::SMEM, attr);
-  split_kernel<64, false, TMAP><<<p.max_items, kThreads, Geo::SMEM, st>>>(p, kmap, vmap);
-  return after_launch("split_kernel");
+  return launch_k("split_kernel", split_kernel<64, false, TMAP>, dim3(p.max_items), dim3(kThreads), Geo::SMEM, st,
+                  pdl, p, kmap, vmap);
 }
 
 static int target_items_for(int num_sms, int occ) {
@@ -492,20 +548,22 @@ static int run_attention(AttnParams p, const CUtensorMap& kmap, const CUtensorMa
     if (int rc = after_launch("plan_kernel")) return rc;
   }
   if (int rc = record_event(ev_begin, stream)) return rc;
+  // programmatic launches overlap each kernel's start with its predecessor's tail;
+  // profiling events between the kernels need ordinary launches
+  const bool pdl = ev_begin == nullptr && ev_end == nullptr;
   int rc = SPECDEC_OK;
   if constexpr (D == 128) {
     const int rows_max = p.n_rep * (p.q_tile < p.max_q_len ? p.q_tile : p.max_q_len);
-    rc = rows_max <= 16 ? launch_verify<16, VF8, TMAP>(p, kmap, vmap, stream)
-                        : launch_verify<32, VF8, TMAP>(p, kmap, vmap, stream);
+    rc = rows_max <= 16 ? launch_verify<16, VF8, TMAP>(p, kmap, vmap, stream, pdl)
+                        : launch_verify<32, VF8, TMAP>(p, kmap, vmap, stream, pdl);
   } else {
-    rc = launch_split64<TMAP>(p, kmap, vmap, stream);
+    rc = launch_split64<TMAP>(p, kmap, vmap, stream, pdl);
   }
   if (rc) return rc;
   if (int rc2 = record_event(ev_end, stream)) return rc2;
   const int rows_max = p.n_rep * (p.q_tile < p.max_q_len ? p.q_tile : p.max_q_len);
   dim3 mgrid(p.max_groups, rows_max < kMaxRows ? rows_max : kMaxRows);
-  merge_kernel<D><<<mgrid, 256, 0, stream>>>(p);
-  return after_launch("merge_kernel");
+  return launch_k("merge_kernel", merge_kernel<D>, mgrid, dim3(256), 0, stream, pdl, p);
 }
 
 static int fill_workspace(AttnParams& p, void* ws, size_t ws_bytes, int B, int KV, int D, int num_sms, int occ) {
@@ -519,6 +577,7 @@ static int fill_workspace(AttnParams& p, void* ws, size_t ws_bytes, int B, int K
   p.hdr = reinterpret_cast<PlanHeader*>(base);
   p.items = reinterpret_cast<WorkItem*>(base + w.items);
   p.groups = reinterpret_cast<GroupInfo*>(base + w.groups);
+  p.cta_first = reinterpret_cast<int32_t*>(base + w.ctas);
   p.p_lse = reinterpret_cast<float*>(base + w.lse);
   p.p_o = reinterpret_cast<float*>(base + w.po);
   p.max_items = w.max_items;

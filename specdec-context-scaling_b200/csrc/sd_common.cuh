@@ -33,6 +33,17 @@ SD_DEV void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
 SD_DEV void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while its
+// predecessor on the stream is still running.  grid_dep_wait() returns once that
+// predecessor has completed and its memory is visible (a no-op for an ordinary
+// launch); every read of device data another kernel produces, and every global
+// write, comes after it.  grid_dep_launch() lets the successor start early; a CTA
+// issues it only after its own grid_dep_wait(), so a kernel that has started can
+// rely on everything before its immediate predecessor having completed.
+SD_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+SD_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 SD_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 SD_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {

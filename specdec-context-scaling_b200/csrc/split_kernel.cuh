@@ -50,6 +50,8 @@ __global__ void __launch_bounds__(kThreads, 1) split_kernel(const AttnParams p,
   __shared__ int s_abort;
   __shared__ int s_issued;
 
+  grid_dep_wait();
+  grid_dep_launch();
   // the header and the item are independent loads: issue both, then test
   const int num_items = p.hdr->num_items;
   const WorkItem it = p.items[blockIdx.x];
