@@ -16,13 +16,13 @@
 //   1. plan_kernel     (1 CTA)   device lengths -> work items (seq, kv head,
 //                                query tile, key-block range) + merge groups.
 //                                One plan serves all layers of a step.
-//   2. split_kernel    (1 CTA per work item) warp 4 streams the item's pages
-//                                with bulk TMA into an 8-deep mbarrier ring;
-//                                warps 0-3 run QK^T and PV on the tensor cores
-//                                (m16n8k16, fp32 accumulate) with an online
-//                                softmax, then merge their key slices in smem.
-//   3. merge_kernel    (1 CTA per (group, row)) log-sum-exp merge of the
-//                                split partials of groups with >1 split.
+//   2. verify_kernel   (head_dim 128; persistent, one CTA per SM over a balanced
+//                                page range) tcgen05 QK^T / PV with TMEM
+//                                accumulators, see verify_kernel.cuh.
+//      split_kernel    (head_dim 64; one CTA per item) mma.sync QK^T / PV with
+//                                an online softmax, see split_kernel.cuh.
+//   3. merge_kernel    (persistent) log-sum-exp merge of the split partials of
+//                                groups with more than one split.
 #include <cudaTypedefs.h>
 
 #include <math.h>
@@ -50,14 +50,17 @@ struct GroupInfo {
 };
 struct PlanHeader {
   int32_t num_items, pages_per_split, num_groups, total_pages;
-  int32_t pad[60];
+  int32_t num_merge_wide;    // split groups with >= kMergeWide splits: merge_list[0 ..)
+  int32_t num_merge_narrow;  // other split groups: merge_list[max_groups - 1], [max_groups - 2], ...
+  int32_t pad[58];
 };
 static_assert(sizeof(PlanHeader) == 256, "plan header is 256 bytes");
 
 constexpr int kMaxRows = 64;  // query rows (n_rep x query positions) per work item
+constexpr int kMergeWide = 16;  // groups with at least this many splits are merged by whole CTAs
 
 struct WsLayout {
-  size_t items, groups, ctas, lse, po, total;
+  size_t items, groups, ctas, mlist, lse, po, total;
   int32_t max_items, max_groups;
 };
 
@@ -68,7 +71,8 @@ static WsLayout ws_layout(int B, int KV, int max_qtiles, int D, int target_items
   w.items = sizeof(PlanHeader);
   w.groups = align_up(w.items + sizeof(WorkItem) * (size_t)w.max_items, 256);
   w.ctas = align_up(w.groups + sizeof(GroupInfo) * (size_t)w.max_groups, 256);
-  w.lse = align_up(w.ctas + sizeof(int32_t) * (size_t)(target_items / 4 + 1), 256);
+  w.mlist = align_up(w.ctas + sizeof(int32_t) * (size_t)(target_items / 4 + 1), 256);
+  w.lse = align_up(w.mlist + sizeof(GroupInfo) * (size_t)w.max_groups, 256);
   w.po = align_up(w.lse + sizeof(float) * kMaxRows * (size_t)w.max_items, 256);
   w.total = align_up(w.po + sizeof(float) * kMaxRows * (size_t)D * w.max_items, 256);
   return w;
@@ -93,6 +97,7 @@ struct AttnParams {
   WorkItem* items;
   GroupInfo* groups;
   int32_t* cta_first;  // [C + 1]: items of persistent CTA c are cta_first[c] .. cta_first[c+1]-1
+  GroupInfo* merge_list;  // [max_groups]: the groups with more than one split (see PlanHeader)
   float* p_lse;
   float* p_o;
   int32_t max_items, max_groups, target_items;
@@ -189,7 +194,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
   auto cta_of = [&](long long pos) { return static_cast<int>(((pos + 1) * C + P - 1) / P) - 1; };
   auto range_lo = [&](int c) { return static_cast<long long>(c) * P / C; };
 
-  int carry = 0;
+  int carry = 0, wcarry = 0, ncarry = 0;
   long long pcarry = 0;
   for (int base = 0; base < ngroups; base += blockDim.x) {
     const int gi = base + threadIdx.x;
@@ -204,6 +209,10 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
     }
     int chunk_total;
     const int first = carry + block_exclusive_scan(n, chunk_total, s_warp);
+    const bool wide = n >= kMergeWide, narrow = n > 1 && !wide;
+    int chunk_wide, chunk_narrow;
+    const int wpos = wcarry + block_exclusive_scan(wide ? 1 : 0, chunk_wide, s_warp);
+    const int npos = ncarry + block_exclusive_scan(narrow ? 1 : 0, chunk_narrow, s_warp);
     if (gi < ngroups) {
       GroupInfo g;
       g.first_item = first;
@@ -214,6 +223,8 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
       g.nq = nq;
       g.pad0 = g.pad1 = 0;
       p.groups[gi] = g;
+      if (wide) p.merge_list[wpos] = g;
+      if (narrow) p.merge_list[p.max_groups - 1 - npos] = g;
     }
     // items of this chunk of groups, written in parallel: item i belongs to the
     // last group whose first item is <= i (empty groups never match)
@@ -253,6 +264,8 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
     }
     __syncthreads();
     carry += chunk_total;
+    wcarry += chunk_wide;
+    ncarry += chunk_narrow;
     pcarry += chunk_pages;
   }
   // first item of every CTA of the grid (items are ordered by CTA): cta_first[c] .. cta_first[c+1]
@@ -268,6 +281,8 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
     p.hdr->num_items = carry;
     p.hdr->pages_per_split = static_cast<int32_t>(C > 0 ? (P + C - 1) / C : 0);
     p.hdr->num_groups = ngroups;
+    p.hdr->num_merge_wide = wcarry;
+    p.hdr->num_merge_narrow = ncarry;
     p.hdr->total_pages = static_cast<int32_t>(P);
   }
 }
@@ -276,84 +291,128 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
 #include "verify_kernel.cuh"
 
 // ---------------------------------------------------------------- merge kernel
-// One CTA per (group, query row) of groups with more than one split; 256 threads =
-// 8 split lanes x 32 dim quads.  The split lse values are loaded in one pass and
-// turned into weights in shared memory, then every lane streams its splits'
-// partial rows with independent loads.
+// Log-sum-exp merge of split partials, persistent over the plan's merge_list (the
+// groups with more than one split).  A unit is one query row of such a group.
+// Rows of groups with >= kMergeWide splits are merged by a whole CTA (its warps
+// take every NWARP-th split and combine in shared memory); the other rows by one
+// warp each.  Lane l owns dims 4(l % NQ) .. +3 of the splits s = l / NQ (mod SPW),
+// so every lane streams float4 partial rows; state is an online (max, sum, acc).
+constexpr int kMergeThreads = 512;
+// Launch-time shared memory that keeps merge CTAs one per SM: launched early behind
+// the attention kernel, they would otherwise pile onto the first SMs it frees.
+constexpr int kMergeSpreadSmem = 120 * 1024;
+
+struct MergeState {
+  float m, l;
+  float4 a;
+};
+SD_DEV void merge_absorb(MergeState& st, float lse, const float4& v) {
+  if (lse == -INFINITY) return;  // empty partial
+  const float m = fmaxf(st.m, lse);
+  const float f = (st.m == -INFINITY) ? 0.f : fast_exp2(st.m - m);
+  const float w = fast_exp2(lse - m);
+  st.a.x = st.a.x * f + v.x * w;
+  st.a.y = st.a.y * f + v.y * w;
+  st.a.z = st.a.z * f + v.z * w;
+  st.a.w = st.a.w * f + v.w * w;
+  st.l = st.l * f + w;
+  st.m = m;
+}
+SD_DEV void merge_combine(MergeState& st, const MergeState& o) {
+  if (o.m == -INFINITY) return;
+  const float m = fmaxf(st.m, o.m);
+  const float f = (st.m == -INFINITY) ? 0.f : fast_exp2(st.m - m);
+  const float g = fast_exp2(o.m - m);
+  st.a.x = st.a.x * f + o.a.x * g;
+  st.a.y = st.a.y * f + o.a.y * g;
+  st.a.z = st.a.z * f + o.a.z * g;
+  st.a.w = st.a.w * f + o.a.w * g;
+  st.l = st.l * f + o.l * g;
+  st.m = m;
+}
+
 template <int D>
-__global__ void __launch_bounds__(256) merge_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(kMergeThreads) merge_kernel(const AttnParams p) {
   grid_dep_wait();
   grid_dep_launch();
-  const int gi = blockIdx.x;
-  if (gi >= p.hdr->num_groups) return;
-  const GroupInfo grp = p.groups[gi];
-  if (grp.nsplit <= 1) return;
-  const int R = p.n_rep * grp.nq;
-  const int r = blockIdx.y;
-  if (r >= R) return;
-  constexpr int NQ = D / 4;
-  constexpr int NL = 256 / NQ;  // split lanes
-  constexpr int MAXW = 1024;
-  __shared__ float s_w[MAXW];
-  __shared__ float s_red[8];
-  __shared__ float4 s_acc[NL][NQ];
-  __shared__ float s_L[NL];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int ns = min(grp.nsplit, MAXW);
-  if (grp.nsplit > MAXW && tid == 0) raise_status(p.status, SPECDEC_STATUS_BAD_LENGTH);
-  float mx = -INFINITY;
-  for (int s = tid; s < ns; s += 256) {
-    const float l = p.p_lse[static_cast<int64_t>(grp.first_item + s) * kMaxRows + r];
-    s_w[s] = l;
-    mx = fmaxf(mx, l);
-  }
+  constexpr int NQ = D / 4;                 // dim quads
+  constexpr int SPW = 32 / NQ;              // split slots per warp
+  constexpr int NWARP = kMergeThreads / 32;
+  __shared__ MergeState s_st[NWARP][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int quad = lane % NQ, slot = lane / NQ;
+  const int RU = p.n_rep * min(p.q_tile, p.max_q_len);  // row slots per group
+  const int wide_units = p.hdr->num_merge_wide * RU;
+  const int narrow_units = p.hdr->num_merge_narrow * RU;
+
+  // the splits s = s0, s0 + step, ... of row r of group grp
+  auto stream = [&](const GroupInfo& grp, int r, int s0, int step, MergeState& st) {
+    st.m = -INFINITY;
+    st.l = 0.f;
+    st.a = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int64_t base = static_cast<int64_t>(grp.first_item) * kMaxRows + r;
+    for (int s = s0; s < grp.nsplit; s += 8 * step) {
+      float lse[8];
+      float4 v[8];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if (lane == 0) s_red[warp] = mx;
-  __syncthreads();
-  float M = s_red[0];
+      for (int k = 0; k < 8; ++k) {
+        const int sk = s + k * step;
+        const bool in = sk < grp.nsplit;
+        lse[k] = in ? p.p_lse[base + static_cast<int64_t>(sk) * kMaxRows] : -INFINITY;
+        v[k] = in ? reinterpret_cast<const float4*>(p.p_o + (base + static_cast<int64_t>(sk) * kMaxRows) * D)[quad]
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
 #pragma unroll
-  for (int w = 1; w < 8; ++w) M = fmaxf(M, s_red[w]);
-  for (int s = tid; s < ns; s += 256) s_w[s] = (M == -INFINITY) ? 0.f : fast_exp2(s_w[s] - M);
-  __syncthreads();
-  const int dq = tid % NQ, sl = tid / NQ;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  float L = 0.f;
-#pragma unroll 4
-  for (int s = sl; s < ns; s += NL) {
-    const float w = s_w[s];
-    const float4 v = *reinterpret_cast<const float4*>(
-        p.p_o + (static_cast<int64_t>(grp.first_item + s) * kMaxRows + r) * D + dq * 4);
-    acc.x += v.x * w;
-    acc.y += v.y * w;
-    acc.z += v.z * w;
-    acc.w += v.w * w;
-    L += w;
-  }
-  s_acc[sl][dq] = acc;
-  if (dq == 0) s_L[sl] = L;
-  __syncthreads();
-  if (sl == 0) {
-    float4 a = s_acc[0][dq];
-    float Lt = s_L[0];
-#pragma unroll
-    for (int k = 1; k < NL; ++k) {
-      const float4 b = s_acc[k][dq];
-      a.x += b.x;
-      a.y += b.y;
-      a.z += b.z;
-      a.w += b.w;
-      Lt += s_L[k];
+      for (int k = 0; k < 8; ++k) merge_absorb(st, lse[k], v[k]);
     }
-    const float inv = Lt > 0.f ? 1.f / Lt : 0.f;
-    const int hh = r / grp.nq, qi = grp.q0 + r % grp.nq;
-    const int row0 = seq_row0(p, grp.b);
-    __nv_bfloat16* dst = p.out + static_cast<int64_t>(row0 + qi) * p.o_st +
-                         static_cast<int64_t>(grp.h * p.n_rep + hh) * p.o_sh + dq * 4;
-    uint2 pk;
-    pk.x = pack_bf16(a.x * inv, a.y * inv);
-    pk.y = pack_bf16(a.z * inv, a.w * inv);
-    *reinterpret_cast<uint2*>(dst) = pk;
+  };
+  auto finish = [&](const GroupInfo& grp, int r, MergeState st) {
+    if (SPW == 2) {
+      MergeState o;
+      o.m = __shfl_xor_sync(0xffffffffu, st.m, 16);
+      o.l = __shfl_xor_sync(0xffffffffu, st.l, 16);
+      o.a.x = __shfl_xor_sync(0xffffffffu, st.a.x, 16);
+      o.a.y = __shfl_xor_sync(0xffffffffu, st.a.y, 16);
+      o.a.z = __shfl_xor_sync(0xffffffffu, st.a.z, 16);
+      o.a.w = __shfl_xor_sync(0xffffffffu, st.a.w, 16);
+      merge_combine(st, o);
+    }
+    if (slot == 0) {
+      const float inv = st.l > 0.f ? 1.f / st.l : 0.f;
+      const int hh = r / grp.nq, qi = grp.q0 + r % grp.nq;
+      __nv_bfloat16* dst = p.out + static_cast<int64_t>(seq_row0(p, grp.b) + qi) * p.o_st +
+                           static_cast<int64_t>(grp.h * p.n_rep + hh) * p.o_sh + quad * 4;
+      uint2 pk;
+      pk.x = pack_bf16(st.a.x * inv, st.a.y * inv);
+      pk.y = pack_bf16(st.a.z * inv, st.a.w * inv);
+      *reinterpret_cast<uint2*>(dst) = pk;
+    }
+  };
+
+  // wide rows: one CTA each
+  for (int u = blockIdx.x; u < wide_units; u += gridDim.x) {
+    const GroupInfo grp = p.merge_list[u / RU];
+    const int r = u % RU;
+    if (r >= p.n_rep * grp.nq) continue;  // uniform per CTA
+    MergeState st;
+    stream(grp, r, warp * SPW + slot, NWARP * SPW, st);
+    s_st[warp][lane] = st;
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll 1
+      for (int w = 1; w < NWARP; ++w) merge_combine(st, s_st[w][lane]);
+      finish(grp, r, st);
+    }
+    __syncthreads();
+  }
+  // narrow rows: one warp each
+  for (int u = blockIdx.x * NWARP + warp; u < narrow_units; u += gridDim.x * NWARP) {
+    const GroupInfo grp = p.merge_list[p.max_groups - 1 - u / RU];
+    const int r = u % RU;
+    if (r >= p.n_rep * grp.nq) continue;  // uniform per warp
+    MergeState st;
+    stream(grp, r, slot, SPW, st);
+    finish(grp, r, st);
   }
 }
 
@@ -561,9 +620,10 @@ static int run_attention(AttnParams p, const CUtensorMap& kmap, const CUtensorMa
   }
   if (rc) return rc;
   if (int rc2 = record_event(ev_end, stream)) return rc2;
-  const int rows_max = p.n_rep * (p.q_tile < p.max_q_len ? p.q_tile : p.max_q_len);
-  dim3 mgrid(p.max_groups, rows_max < kMaxRows ? rows_max : kMaxRows);
-  return launch_k("merge_kernel", merge_kernel<D>, mgrid, dim3(256), 0, stream, pdl, p);
+  static bool mattr[64] = {};
+  set_smem_attr(merge_kernel<D>, kMergeSpreadSmem, mattr);
+  return launch_k("merge_kernel", merge_kernel<D>, dim3(p.target_items / 4), dim3(kMergeThreads), kMergeSpreadSmem,
+                  stream, pdl, p);
 }
 
 static int fill_workspace(AttnParams& p, void* ws, size_t ws_bytes, int B, int KV, int D, int num_sms, int occ) {
@@ -578,6 +638,7 @@ static int fill_workspace(AttnParams& p, void* ws, size_t ws_bytes, int B, int K
   p.items = reinterpret_cast<WorkItem*>(base + w.items);
   p.groups = reinterpret_cast<GroupInfo*>(base + w.groups);
   p.cta_first = reinterpret_cast<int32_t*>(base + w.ctas);
+  p.merge_list = reinterpret_cast<GroupInfo*>(base + w.mlist);
   p.p_lse = reinterpret_cast<float*>(base + w.lse);
   p.p_o = reinterpret_cast<float*>(base + w.po);
   p.max_items = w.max_items;

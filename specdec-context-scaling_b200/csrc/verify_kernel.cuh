@@ -2,13 +2,15 @@
 // tensor cores (tcgen05, TMEM accumulators) for head_dim 128.  Included inside
 // namespace sd by paged_attention.cu, after split_kernel.cuh.
 //
-// One CTA per work item (sequence b, KV head h, key range), 192 threads:
-//   warps 0-3  softmax + epilogue; thread t owns key t of each 128-key tile (TMEM
-//              lane t) and, in the epilogue, output dim t
-//   warp 4     producer: bulk-TMA copies of the item's pages into an NS-deep ring of
+// Persistent CTAs (one per SM) over a balanced page range, 320 threads:
+//   warps 0-7  softmax + epilogue; warp w owns keys 32 (w % 4) .. +31 of each
+//              128-key tile (TMEM lane quarter w % 4) for the query rows of half
+//              w / 4, and in the epilogue output dims 32 (w % 4) .. +31 of those rows
+//   warp 8     producer: bulk-TMA copies of the pages into an NS-deep ring of
 //              128-key tiles (K [2 halves][128 rows][128 B] in the 128-byte-swizzled
-//              image of the pool; V likewise, or raw E4M3 rows + per-token scales)
-//   warp 5     MMA issuer (one lane) and owner of the TMEM allocation
+//              image of the pool; V likewise, or raw E4M3 rows + per-token scales),
+//              and the Q rows of each item
+//   warp 9     MMA issuer (one lane) and owner of the TMEM allocation
 // Per tile t (buffer b = t & 1):
 //   S^T[b] (128 keys x NR rows, fp32, TMEM)  = K_tile . Q^T            (8 x K=16 MMAs)
 //   softmax warps: row maxima over the tile, lazy online rescale of O (only when a
@@ -20,7 +22,10 @@
 // Rows: the n_rep query heads x q query positions of one KV head (NR = 16 or 32).
 #pragma once
 
-constexpr int kV3Threads = 192;
+constexpr int kSmWarps = 8;                    // softmax warps: (key quarter, row half)
+constexpr int kProducerWarp = kSmWarps;        // bulk-TMA producer
+constexpr int kMmaWarp = kSmWarps + 1;         // MMA issuer, TMEM owner
+constexpr int kV3Threads = 32 * (kSmWarps + 2);
 constexpr int kTileKeys = 128;
 constexpr int kTilePages = 8;
 constexpr float kRescaleLog2 = 8.f;   // lazy rescale threshold (log2 units)
