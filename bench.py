@@ -44,6 +44,9 @@ METRIC = "verify-attn HBM GB/s (% of 8 TB/s) at 2K–8K ctx; SpecDec decode toke
 H, KV, D = 12, 2, 128
 LAYERS = 28
 PAGE = 16
+# DRAM bytes (read + write) of one verify-kernel launch of the headline workload, from an
+# `ncu --set full` capture of `bench.py --profile-case verify8k` (8,482,816 read + 0 written)
+NCU_TRAFFIC_VERIFY8K = 8482816
 
 
 def attn_bytes(T: int, q: int, fp8: bool, heads: int = H) -> float:
@@ -473,7 +476,9 @@ def run_ours(args, world, rank, local):
                        "l2": "inputs larger than L2: 28 distinct layer caches = 235 MB read per step"},
             "pct_of_8TBs_per_gpu": round(value / world / 80.0, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "frac": round(achieved / peak, 4), "traffic": NCU_TRAFFIC_VERIFY8K,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch, "
+                                           "bench.py --profile-case verify8k",
                          "kernel": "verify_kernel<32,bf16V,pool> (tcgen05)", "peak_kind": peak_kind,
                          "algorithmic_bytes_per_launch": per_call,
                          "launch_ms": round(split_ms, 5)},
@@ -486,6 +491,34 @@ def run_ours(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def run_profile_case(args):
+    """Replays one workload's step graph (no timing, no JSON): the command profilers capture."""
+    import torch
+
+    from specdec_b200 import _lib
+
+    _lib.load_library()
+    if args.profile_case == "verify8k":
+        cache = filled_cache(LAYERS, [8192], False, 0)
+        step = GraphStep(cache, [5], [8192], 0)
+    else:
+        g = torch.Generator().manual_seed(4)
+        lens = [int(x) for x in torch.randint(1024, 8193, (64,), generator=g)]
+        q_lens = [1, 5] * 32
+        perm = torch.randperm(64, generator=g).tolist()
+        q_lens = [q_lens[i] for i in perm]
+        cache = filled_cache(2, lens, args.profile_case == "ragged64", 4)
+        step = GraphStep(cache, q_lens, lens, 4)
+    for _ in range(args.warmup + args.steps):
+        step.replay()
+    torch.cuda.synchronize()
+    st = int(step.status.item())
+    if st:
+        raise RuntimeError(f"device status {st:#x}: {_lib.status_message(st)}")
+    print(f"profile case {args.profile_case}: {args.warmup + args.steps} replays, "
+          f"{step.launches_per_step} launches per replay", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -493,7 +526,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true", help="headline line only (no extra configs/e2e/cpu)")
+    ap.add_argument("--profile-case", choices=["verify8k", "ragged64", "ragged64-bf16"], default=None,
+                    help="only replay this workload's step graph warmup + steps times (for profilers)")
     args = ap.parse_args()
+    if args.profile_case:
+        run_profile_case(args)
+        return
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))
