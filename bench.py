@@ -343,6 +343,38 @@ def measure_e2e(steps, warmup, T=8192, q=5, layers=LAYERS, seed=0):
     return layers * attn_bytes(T, q, False) * steps / (ms * 1e-3) / 1e9, ms / steps, h2d, d2h
 
 
+def measure_specdec(args, world, rank):
+    """greedy SpecDec with random-init Qwen2.5-1.5B (target) and
+    Qwen2.5-0.5B (draft) geometries, args.specdec_seqs sequences with uniform-random
+    prompts of args.specdec_prompt tokens, k = 4, args.specdec_new tokens each, sharded
+    data-parallel over the ranks (one all-gather of tokens at the end).  Decode tokens/s
+    counts the tokens emitted by decode rounds (the prompt pass's first token excluded)
+    over the max-over-ranks device time of the round-graph replays."""
+    import torch
+
+    from specdec_b200.engine.dp import run_specdec_dp
+    from specdec_b200.engine.model import QWEN25_0P5B, QWEN25_1P5B
+
+    res = run_specdec_dp(QWEN25_1P5B, QWEN25_0P5B, total_seqs=args.specdec_seqs, prompt_len=args.specdec_prompt,
+                         max_new=args.specdec_new, k=4, seed=0, world=world, rank=rank, target_v="e4m3",
+                         barrier=lambda: barrier(world))
+    decode_tokens = args.specdec_seqs * (args.specdec_new - 1)
+    out = {
+        "decode_tokens_per_s": round(decode_tokens / res.decode_s, 1),
+        "decode_s": round(res.decode_s, 4),
+        "prefill_s": round(res.prefill_s, 3),
+        "rounds": res.rounds,
+        "accepted_per_round": round(res.acceptance, 3),
+        "sequences": args.specdec_seqs, "prompt_len": args.specdec_prompt, "new_tokens": args.specdec_new,
+        "k": 4, "n_gpus": world, "parallelism": f"dp{world}", "kv": "bf16 K / E4M3 V (target), bf16 (draft)",
+        "weights": "random-init bf16 (seeded, identical on every rank)",
+        "tokens_checksum": int(res.tokens.long().sum()),
+    }
+    del res
+    torch.cuda.empty_cache()
+    return out
+
+
 def cpu_reference(calls_budget_s: float = 12.0, min_calls: int = 3, T=8192, q=5, max_calls=None):
     """The reference's eager attention formula on the host (CPU oracle), all threads.
 
@@ -457,6 +489,9 @@ def run_ours(args, world, rank, local):
                "path": "ops.append_kv + ops.paged_attention per layer (ctypes C ABI), pinned host q/k/v in, out back"}
         e_ms_max = max_over_ranks(e_ms, world)
         e2e["value"] = round(world * LAYERS * per_call / (e_ms_max * 1e-3) / 1e9, 3)
+    specdec = None
+    if not args.no_specdec:
+        specdec = measure_specdec(args, world, rank)
     if rank == 0 and not args.no_extras:
         c_gbs, calls, el, thr = cpu_reference()
         cpu = {"value": round(c_gbs, 3), "unit": "GB/s", "cores": thr, "kind": "port",
@@ -487,6 +522,7 @@ def run_ours(args, world, rank, local):
             "gpu_launches": launches,
             "clocks": clk.summary(),
             "extras": extras,
+            "specdec_e2e": specdec,
         }
         print(json.dumps(line), flush=True)
 
@@ -526,6 +562,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true", help="headline line only (no extra configs/e2e/cpu)")
+    ap.add_argument("--no-specdec", action="store_true", help="skip the end-to-end SpecDec tokens/s measurement")
+    ap.add_argument("--specdec-seqs", type=int, default=256)
+    ap.add_argument("--specdec-prompt", type=int, default=8192)
+    ap.add_argument("--specdec-new", type=int, default=64)
     ap.add_argument("--profile-case", choices=["verify8k", "ragged64", "ragged64-bf16"], default=None,
                     help="only replay this workload's step graph warmup + steps times (for profilers)")
     args = ap.parse_args()
