@@ -16,11 +16,9 @@
 //   1. plan_kernel     (1 CTA)   device lengths -> work items (seq, kv head,
 //                                query tile, key-block range) + merge groups.
 //                                One plan serves all layers of a step.
-//   2. verify_kernel   (head_dim 128; persistent, one CTA per SM over a balanced
-//                                page range) tcgen05 QK^T / PV with TMEM
+//   2. verify_kernel   (head_dim 64 / 128; persistent, one CTA per SM over a
+//                                balanced page range) tcgen05 QK^T / PV with TMEM
 //                                accumulators, see verify_kernel.cuh.
-//      split_kernel    (head_dim 64; one CTA per item) mma.sync QK^T / PV with
-//                                an online softmax, see split_kernel.cuh.
 //   3. merge_kernel    (persistent) log-sum-exp merge of the split partials of
 //                                groups with more than one split.
 #include <cudaTypedefs.h>
@@ -101,7 +99,7 @@ struct AttnParams {
   float* p_lse;
   float* p_o;
   int32_t max_items, max_groups, target_items;
-  int32_t tile_pages;  // the split kernel consumes keys in tiles of this many pages
+  int32_t tile_pages;  // the verify kernel consumes keys in tiles of this many pages
   int32_t* status;
 };
 
@@ -287,7 +285,6 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
   }
 }
 
-#include "split_kernel.cuh"
 #include "verify_kernel.cuh"
 
 // ---------------------------------------------------------------- merge kernel
@@ -516,13 +513,17 @@ static int encode_kv_map(CUtensorMap* map, const void* base, int planes, int T, 
   return SPECDEC_OK;
 }
 
-// Query positions per work item: rows (n_rep x positions) must fit the split
-// kernel's row tile -- 32 rows for the tcgen05 kernel (head_dim 128), 64 otherwise.
+// Query positions per work item: rows (n_rep x positions) must fit the verify
+// kernel's row tile of 32 (TMEM columns of S and O).
 static int q_tile_for(int n_rep, int D) {
-  const int rows = (D == 128) ? 32 : kMaxRows;
+  (void)D;
+  constexpr int rows = 32;
   return n_rep >= rows ? 1 : rows / n_rep;
 }
-static int tile_pages_for(int D) { return D == 128 ? kTilePages : 1; }
+static int tile_pages_for(int D) {
+  (void)D;
+  return kTilePages;
+}
 
 // dynamic shared memory opt-in, once per (kernel, device)
 template <typename K>
@@ -557,25 +558,15 @@ static int launch_k(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 bl
   return after_launch(what);
 }
 
-template <int NR, bool VF8, bool TMAP>
+template <int NR, bool VF8, bool TMAP, int D>
 static int launch_verify(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, cudaStream_t st,
                          bool pdl) {
-  using Geo = V3Geom<NR, VF8>;
+  using Geo = V3Geom<NR, VF8, D>;
   static bool attr[64] = {};
-  set_smem_attr(verify_kernel<NR, VF8, TMAP>, Geo::SMEM, attr);
+  set_smem_attr(verify_kernel<NR, VF8, TMAP, D>, Geo::SMEM, attr);
   // persistent: one CTA per SM, the plan's C = target_items / 4 ranges
   const int grid = p.target_items / 4;
-  return launch_k("verify_kernel", verify_kernel<NR, VF8, TMAP>, dim3(grid), dim3(kV3Threads), Geo::SMEM, st,
-                  pdl, p, kmap, vmap);
-}
-
-template <bool TMAP>
-static int launch_split64(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, cudaStream_t st,
-                          bool pdl) {
-  using Geo = StageGeom<64, false>;
-  static bool attr[64] = {};
-  set_smem_attr(split_kernel<64, false, TMAP>, Geo::SMEM, attr);
-  return launch_k("split_kernel", split_kernel<64, false, TMAP>, dim3(p.max_items), dim3(kThreads), Geo::SMEM, st,
+  return launch_k("verify_kernel", verify_kernel<NR, VF8, TMAP, D>, dim3(grid), dim3(kV3Threads), Geo::SMEM, st,
                   pdl, p, kmap, vmap);
 }
 
@@ -610,14 +601,9 @@ static int run_attention(AttnParams p, const CUtensorMap& kmap, const CUtensorMa
   // programmatic launches overlap each kernel's start with its predecessor's tail;
   // profiling events between the kernels need ordinary launches
   const bool pdl = ev_begin == nullptr && ev_end == nullptr;
-  int rc = SPECDEC_OK;
-  if constexpr (D == 128) {
-    const int rows_max = p.n_rep * (p.q_tile < p.max_q_len ? p.q_tile : p.max_q_len);
-    rc = rows_max <= 16 ? launch_verify<16, VF8, TMAP>(p, kmap, vmap, stream, pdl)
-                        : launch_verify<32, VF8, TMAP>(p, kmap, vmap, stream, pdl);
-  } else {
-    rc = launch_split64<TMAP>(p, kmap, vmap, stream, pdl);
-  }
+  const int rows_max = p.n_rep * (p.q_tile < p.max_q_len ? p.q_tile : p.max_q_len);
+  const int rc = rows_max <= 16 ? launch_verify<16, VF8, TMAP, D>(p, kmap, vmap, stream, pdl)
+                                : launch_verify<32, VF8, TMAP, D>(p, kmap, vmap, stream, pdl);
   if (rc) return rc;
   if (int rc2 = record_event(ev_end, stream)) return rc2;
   static bool mattr[64] = {};
@@ -664,8 +650,8 @@ static int validate_paged(const SpecdecAttnArgs* a) {
   if (bt.num_seqs <= 0 || bt.num_q_heads <= 0 || kv.num_kv_heads <= 0)
     return fail(SPECDEC_ERR_INVALID, "num_seqs, num_q_heads and num_kv_heads must be positive");
   if (bt.num_q_heads % kv.num_kv_heads != 0) return fail(SPECDEC_ERR_INVALID, "query heads must divide KV heads");
-  if (bt.num_q_heads / kv.num_kv_heads > (kv.head_dim == 128 ? 32 : kMaxRows))
-    return fail(SPECDEC_ERR_UNSUPPORTED, "too many query heads per KV head (32 for head_dim 128, %d for 64)", kMaxRows);
+  if (bt.num_q_heads / kv.num_kv_heads > 32)
+    return fail(SPECDEC_ERR_UNSUPPORTED, "at most 32 query heads per KV head");
   if (kv.head_dim != 64 && kv.head_dim != 128) return fail(SPECDEC_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
   if (kv.v_dtype != SPECDEC_BF16 && kv.v_dtype != SPECDEC_E4M3)
     return fail(SPECDEC_ERR_UNSUPPORTED, "v_dtype must be SPECDEC_BF16 or SPECDEC_E4M3");
@@ -865,7 +851,7 @@ extern "C" int specdec_attention(const void* q, const void* k, const void* v, vo
   p.KV = KV;
   p.n_rep = H / KV;
   if (p.n_rep > kMaxRows) return fail(SPECDEC_ERR_UNSUPPORTED, "more than %d query heads per KV head", kMaxRows);
-  if (D == 128 && p.n_rep > 32) return fail(SPECDEC_ERR_UNSUPPORTED, "head_dim 128 supports at most 32 query heads per KV head");
+  if (p.n_rep > 32) return fail(SPECDEC_ERR_UNSUPPORTED, "at most 32 query heads per KV head");
   p.max_q_len = S;
   p.q_tile = q_tile_for(p.n_rep, D);
   p.tile_pages = tile_pages_for(D);
