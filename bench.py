@@ -230,8 +230,10 @@ class GraphStep:
 
         ops.ragged_plan(self.q[0], self.cache, self.batch, self.ws, status=self.status)
         for layer in range(self.cache.num_layers):
+            # layer 0 follows the plan kernel directly; later layers follow attention
+            # kernels, which write no KV, page table or plan: their loads may start early
             ops.paged_attention(self.q[layer], self.cache, layer, self.batch, out=self.out[layer], workspace=self.ws,
-                                reuse_plan=True, status=self.status,
+                                reuse_plan=True, status=self.status, history_ready=layer > 0,
                                 split_events=None if self.events is None else self.events[layer])
 
     def replay(self):

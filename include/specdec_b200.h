@@ -39,7 +39,7 @@ extern "C" {
 
 typedef struct CUstream_st* specdec_stream_t; /* == cudaStream_t */
 
-#define SPECDEC_ABI_VERSION 1
+#define SPECDEC_ABI_VERSION 2
 #define SPECDEC_PAGE_TOKENS 16 /* tokens per KV page */
 
 typedef enum SpecdecResult {
@@ -118,12 +118,21 @@ typedef struct SpecdecAttnArgs {
   int32_t* status;      /* device int32, may be NULL */
   int32_t reuse_plan;   /* 1: the workspace already holds the plan for this batch
                            (built by specdec_ragged_plan or an earlier call) */
-  int32_t num_sms;      /* 0: query the device */
+  int32_t num_sms;      /* SMs the call may use; 0 or more than the device has: all of them
+                           (the attention kernel runs one CTA per SM and its CTAs synchronise,
+                           so all of them must fit on the device at once) */
   /* Optional profiling hook: cudaEvent_t handles recorded on `stream` right before
      and right after the split-KV kernel (as external event nodes under stream
      capture).  NULL = no events. */
   void* split_event_begin;
   void* split_event_end;
+  /* 1: the caller promises that the KV history of every sequence (positions below
+     ctx_len - q_len), the page table and, with reuse_plan, the plan are final when
+     this call is enqueued -- the work immediately before it on the stream writes none
+     of them.  The kernel then starts loading them while that work finishes (Q is
+     still read, and outputs written, only after it).  0: nothing is read early. */
+  int32_t history_ready;
+  int32_t reserved0;
 } SpecdecAttnArgs;
 
 /* Bytes of workspace (plan + split-KV partials) for a batch of this shape. */

@@ -19,8 +19,8 @@
 //   2. verify_kernel   (head_dim 64 / 128; persistent, one CTA per SM over a
 //                                balanced page range) tcgen05 QK^T / PV with TMEM
 //                                accumulators, see verify_kernel.cuh.
-//   3. merge_kernel    (persistent) log-sum-exp merge of the split partials of
-//                                groups with more than one split.
+//      The same kernel merges the split partials of groups with more than one
+//      split after a grid barrier (merge_splits).
 #include <cudaTypedefs.h>
 
 #include <math.h>
@@ -50,7 +50,9 @@ struct PlanHeader {
   int32_t num_items, pages_per_split, num_groups, total_pages;
   int32_t num_merge_wide;    // split groups with >= kMergeWide splits: merge_list[0 ..)
   int32_t num_merge_narrow;  // other split groups: merge_list[max_groups - 1], [max_groups - 2], ...
-  int32_t pad[58];
+  int32_t pad0[26];
+  unsigned long long bar_arrive;  // grid-barrier arrivals of the verify kernel (own 128-byte line)
+  int32_t pad1[30];
 };
 static_assert(sizeof(PlanHeader) == 256, "plan header is 256 bytes");
 
@@ -100,6 +102,7 @@ struct AttnParams {
   float* p_o;
   int32_t max_items, max_groups, target_items;
   int32_t tile_pages;  // the verify kernel consumes keys in tiles of this many pages
+  int32_t early_loads;  // 1: plan, page table and KV history may be read before the dependency wait
   int32_t* status;
 };
 
@@ -279,26 +282,23 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
     p.hdr->num_items = carry;
     p.hdr->pages_per_split = static_cast<int32_t>(C > 0 ? (P + C - 1) / C : 0);
     p.hdr->num_groups = ngroups;
+    p.hdr->bar_arrive = 0ull;
     p.hdr->num_merge_wide = wcarry;
     p.hdr->num_merge_narrow = ncarry;
     p.hdr->total_pages = static_cast<int32_t>(P);
   }
 }
 
-#include "verify_kernel.cuh"
-
-// ---------------------------------------------------------------- merge kernel
-// Log-sum-exp merge of split partials, persistent over the plan's merge_list (the
-// groups with more than one split).  A unit is one query row of such a group.
-// Rows of groups with >= kMergeWide splits are merged by a whole CTA (its warps
-// take every NWARP-th split and combine in shared memory); the other rows by one
-// warp each.  Lane l owns dims 4(l % NQ) .. +3 of the splits s = l / NQ (mod SPW),
-// so every lane streams float4 partial rows; state is an online (max, sum, acc).
-constexpr int kMergeThreads = 512;
-// Launch-time shared memory that keeps merge CTAs one per SM: launched early behind
-// the attention kernel, they would otherwise pile onto the first SMs it frees.
-constexpr int kMergeSpreadSmem = 120 * 1024;
-
+// ---------------------------------------------------------------- split merge
+// Log-sum-exp merge of split partials, run by the verify kernel's CTAs once every
+// CTA has written its partials (after its grid barrier).  A unit is one query row
+// of a group in the plan's merge_list (the groups with more than one split).  Rows
+// of groups with >= kMergeWide splits are merged by a whole CTA (its warps take
+// every NWARP-th split and combine in shared memory); the other rows by one warp
+// each.  Lane l owns dims 4(l % NQ) .. +3 of the splits s = l / NQ (mod SPW), so
+// every lane streams float4 partial rows; the state is an online (max, sum, acc).
+// Partials come from other CTAs of the same launch, so they are read with
+// L1-bypassing loads.
 struct MergeState {
   float m, l;
   float4 a;
@@ -328,15 +328,11 @@ SD_DEV void merge_combine(MergeState& st, const MergeState& o) {
   st.m = m;
 }
 
-template <int D>
-__global__ void __launch_bounds__(kMergeThreads) merge_kernel(const AttnParams p) {
-  grid_dep_wait();
-  grid_dep_launch();
-  constexpr int NQ = D / 4;                 // dim quads
-  constexpr int SPW = 32 / NQ;              // split slots per warp
-  constexpr int NWARP = kMergeThreads / 32;
-  __shared__ MergeState s_st[NWARP][32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+// s_st: NWARP x 32 states of shared memory (the caller's free staging area)
+template <int D, int NWARP>
+SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int warp, int lane) {
+  constexpr int NQ = D / 4;     // dim quads
+  constexpr int SPW = 32 / NQ;  // split slots per warp
   const int quad = lane % NQ, slot = lane / NQ;
   const int RU = p.n_rep * min(p.q_tile, p.max_q_len);  // row slots per group
   const int wide_units = p.hdr->num_merge_wide * RU;
@@ -355,8 +351,9 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const AttnParams p
       for (int k = 0; k < 8; ++k) {
         const int sk = s + k * step;
         const bool in = sk < grp.nsplit;
-        lse[k] = in ? p.p_lse[base + static_cast<int64_t>(sk) * kMaxRows] : -INFINITY;
-        v[k] = in ? reinterpret_cast<const float4*>(p.p_o + (base + static_cast<int64_t>(sk) * kMaxRows) * D)[quad]
+        lse[k] = in ? __ldcg(p.p_lse + base + static_cast<int64_t>(sk) * kMaxRows) : -INFINITY;
+        v[k] = in ? __ldcg(reinterpret_cast<const float4*>(p.p_o + (base + static_cast<int64_t>(sk) * kMaxRows) * D) +
+                           quad)
                   : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
@@ -393,11 +390,11 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const AttnParams p
     if (r >= p.n_rep * grp.nq) continue;  // uniform per CTA
     MergeState st;
     stream(grp, r, warp * SPW + slot, NWARP * SPW, st);
-    s_st[warp][lane] = st;
+    s_st[warp * 32 + lane] = st;
     __syncthreads();
     if (warp == 0) {
 #pragma unroll 1
-      for (int w = 1; w < NWARP; ++w) merge_combine(st, s_st[w][lane]);
+      for (int w = 1; w < NWARP; ++w) merge_combine(st, s_st[w * 32 + lane]);
       finish(grp, r, st);
     }
     __syncthreads();
@@ -412,6 +409,30 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(const AttnParams p
     finish(grp, r, st);
   }
 }
+
+// Grid-wide barrier of the persistent verify kernel: its grid is at most one CTA per
+// SM at one CTA per SM, so every CTA is resident once the kernel's CTAs run.  The
+// arrival counter grows by the grid size per launch (the plan zeroes it): a CTA that
+// arrives as number `old` waits for the counter to reach the next multiple of the
+// grid size.  Only CTAs with merge work wait.  Called by one thread per CTA;
+// bounded: false after ~1 s.
+SD_DEV bool grid_barrier(PlanHeader* h, unsigned n_ctas, bool wait) {
+  __threadfence();  // this CTA's partials before its arrival
+  const unsigned long long old = atomicAdd(&h->bar_arrive, 1ull);
+  if (!wait) return true;
+  const unsigned long long target = (old / n_ctas + 1) * n_ctas;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    unsigned long long now;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(now) : "l"(&h->bar_arrive) : "memory");
+    if (now >= target) break;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    __nanosleep(64);
+  }
+  return true;
+}
+
+#include "verify_kernel.cuh"
 
 // ---------------------------------------------------------------- fp32 contiguous path
 // CUDA-core kernel for the f32 dtype of the reference op (attention.cu:262-272).
@@ -570,6 +591,13 @@ static int launch_verify(const AttnParams& p, const CUtensorMap& kmap, const CUt
                   pdl, p, kmap, vmap);
 }
 
+// CTAs of the persistent verify kernel: the caller's SM budget, at most the device's
+// SM count (its CTAs meet at a grid barrier, so all of them must be resident at once)
+static int sm_budget(int requested) {
+  const int dev = device_sm_count();
+  return (requested > 0 && requested < dev) ? requested : dev;
+}
+
 static int target_items_for(int num_sms, int occ) {
   // the plan makes at most ~4 waves of one-CTA-per-SM items (see plan_kernel);
   // this bound sizes the workspace and never depends on a device query
@@ -605,11 +633,7 @@ static int run_attention(AttnParams p, const CUtensorMap& kmap, const CUtensorMa
   const int rc = rows_max <= 16 ? launch_verify<16, VF8, TMAP, D>(p, kmap, vmap, stream, pdl)
                                 : launch_verify<32, VF8, TMAP, D>(p, kmap, vmap, stream, pdl);
   if (rc) return rc;
-  if (int rc2 = record_event(ev_end, stream)) return rc2;
-  static bool mattr[64] = {};
-  set_smem_attr(merge_kernel<D>, kMergeSpreadSmem, mattr);
-  return launch_k("merge_kernel", merge_kernel<D>, dim3(p.target_items / 4), dim3(kMergeThreads), kMergeSpreadSmem,
-                  stream, pdl, p);
+  return record_event(ev_end, stream);
 }
 
 static int fill_workspace(AttnParams& p, void* ws, size_t ws_bytes, int B, int KV, int D, int num_sms, int occ) {
@@ -706,7 +730,7 @@ static int paged_entry(const SpecdecAttnArgs* a, cudaStream_t stream, bool plan_
   AttnParams p = params_from(a);
   const int D = a->kv.head_dim;
   const bool vf8 = a->kv.v_dtype == SPECDEC_E4M3;
-  const int sms = a->num_sms > 0 ? a->num_sms : device_sm_count();
+  const int sms = sm_budget(a->num_sms);
   if (int rc = fill_workspace(p, a->workspace, a->workspace_bytes, p.B, p.KV, D, sms, occupancy_for(D, vf8, false)))
     return rc;
   if (plan_only) {
@@ -716,6 +740,9 @@ static int paged_entry(const SpecdecAttnArgs* a, cudaStream_t stream, bool plan_
   CUtensorMap dummy;
   memset(&dummy, 0, sizeof(dummy));
   const bool build = a->reuse_plan == 0;
+  // early loads need a plan from an earlier call (one built now is written by the
+  // kernel right before) and the caller's promise about the history
+  p.early_loads = (!build && a->history_ready != 0) ? 1 : 0;
   void* eb = a->split_event_begin;
   void* ee = a->split_event_end;
   if (D == 128) {
@@ -789,7 +816,7 @@ extern "C" int specdec_paged_attention_noalloc(const SpecdecAttnArgs* args, spec
   const int n_rep = args->batch.num_q_heads / args->kv.num_kv_heads;
   const int qt = q_tile_for(n_rep, args->kv.head_dim);
   const int max_qtiles = (args->batch.max_q_len + qt - 1) / qt;
-  const int sms = args->num_sms > 0 ? args->num_sms : device_sm_count();
+  const int sms = sm_budget(args->num_sms);
   const size_t need =
       ws_layout(args->batch.num_seqs, args->kv.num_kv_heads, max_qtiles, args->kv.head_dim, target_items_for(sms, 0))
           .total;

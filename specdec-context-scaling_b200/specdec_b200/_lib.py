@@ -15,7 +15,7 @@ LIB_NAME = "libspecdec_b200.so"
 LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
 
 PAGE_TOKENS = 16
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 F32, BF16, E4M3 = 0, 1, 2
 
@@ -88,6 +88,8 @@ class AttnArgs(ctypes.Structure):
         ("num_sms", _i32),
         ("split_event_begin", _vp),
         ("split_event_end", _vp),
+        ("history_ready", _i32),
+        ("reserved0", _i32),
     ]
 
 

@@ -207,8 +207,10 @@ class PagedModel:
             ops.append_kv(k[0].transpose(0, 1), v.transpose(0, 1), cache, li, row0=layout.q_row0,
                           n_new=layout.q_len, pos0=layout.pos0, max_new=layout.q_max, status=status)
             o = torch.zeros(rows, c.heads, c.head_dim, dtype=x.dtype, device=x.device)
+            # layers after the first reuse layer 0's plan; the only KV the steps before write
+            # is this step's new tokens, so the history may be loaded early
             ops.paged_attention(q[0].transpose(0, 1), cache, li, layout.batch, out=o, workspace=workspace,
-                                reuse_plan=li > 0, status=status)
+                                reuse_plan=li > 0, status=status, history_ready=li > 0)
             x = x + o.view(rows, c.heads * c.head_dim) @ L.w_o.t()
             x = self._mlp(L, x)
         return ops.rmsnorm(x, self.norm, c.eps)

@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_abi_version(lib):
-    assert lib.specdec_abi_version() == 1
+    assert lib.specdec_abi_version() == 2
 
 
 def test_workspace_sizes_are_host_only(lib):
@@ -94,7 +94,7 @@ def test_struct_layouts_match_c():
 
     assert ctypes.sizeof(_lib.PagedKV) == 56
     assert ctypes.sizeof(_lib.Batch) == 40
-    assert ctypes.sizeof(_lib.AttnArgs) == 8 * 2 + 8 * 4 + 40 + 56 + 8 + 8 + 8 + 8 + 8 + 16
+    assert ctypes.sizeof(_lib.AttnArgs) == 8 * 2 + 8 * 4 + 40 + 56 + 8 + 8 + 8 + 8 + 8 + 16 + 8
 
 
 def test_ops_reject_other_backends():

@@ -105,6 +105,26 @@ def test_plan_reuse_across_layers():
     assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("fp8,D", [(False, 128), (True, 128), (False, 64)])
+def test_history_ready_gives_identical_results(fp8, D):
+    """Loading the plan, page table and KV history before the dependency wait changes
+    no result: a layer stack with history_ready equals the same calls without it."""
+    ops = _ops()
+    lens, q_lens = [900, 4100, 33, 2000], [5, 1, 2, 5]
+    H = 12 if D == 128 else 14
+    cache, ks, vrefs = build_cache(lens, 2, D, fp8=fp8, seed=9, num_layers=3)
+    batch = ops.RaggedBatch.from_lengths(q_lens, lens)
+    q = torch.randn(batch.total_rows, H, D, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).cuda()
+    ws = ops.attn_workspace(batch, H, cache)
+    ops.ragged_plan(q, cache, batch, ws)
+    early = [ops.paged_attention(q, cache, layer, batch, workspace=ws, reuse_plan=True, history_ready=layer > 0)
+             for layer in range(3)]
+    plain = [ops.paged_attention(q, cache, layer, batch) for layer in range(3)]
+    torch.cuda.synchronize()
+    for a, b in zip(early, plain):
+        assert torch.equal(a, b)
+
+
 def test_bad_page_id_sets_status_without_fault():
     """A corrupted page table (host-side) is caught by the producer's bounds check."""
     from specdec_b200 import _lib
