@@ -268,6 +268,12 @@ int specdec_swiglu(const void* gate, const void* up, void* out, int32_t dtype, i
    tcgen05 MMAs from 128-byte-swizzled shared memory into TMEM,
    out1[128][32] = k[128][128] . q[32][128]^T and out2[128][32] = v[128][128]^T . p[32][128]^T
    (bf16 row-major inputs, fp32 outputs) -- the operand layouts of the verify kernel. */
+/* TMA gather self-check (no counterpart in the reference): one CTA fetches rows
+   rows[0..3] of a [n_rows][2048 B] tensor `big` and of a [n_rows][64 B] tensor `small`
+   with one four-row tensor gather each -- the page-row loads of the attention kernel --
+   and writes the 4 x 2048 + 4 x 64 bytes received to `out`. */
+int specdec_gather4_selftest(const void* big, const void* small, int64_t n_rows, const int32_t* rows, void* out,
+                             int32_t* status, specdec_stream_t stream);
 int specdec_umma_selftest(const void* k, const void* q, const void* v, const void* p, float* out1, float* out2,
                           int32_t* status, specdec_stream_t stream);
 const char* specdec_last_error(void);

@@ -534,6 +534,24 @@ static int encode_kv_map(CUtensorMap* map, const void* base, int planes, int T, 
   return SPECDEC_OK;
 }
 
+// 2-D map over `n_rows` contiguous rows of `row_bytes` bytes (64-bit elements, no
+// swizzle) whose box is one row: the shape tile::gather4 loads fetch four rows of.
+static int encode_rows_map(CUtensorMap* map, const void* base, uint64_t n_rows, uint32_t row_bytes) {
+  auto fn = get_encode_fn();
+  if (!fn) return fail(SPECDEC_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if (row_bytes % 16 || row_bytes / 8 > 256 || n_rows == 0)
+    return fail(SPECDEC_ERR_INVALID, "row map: bad row size %u", row_bytes);
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes / 8), static_cast<cuuint64_t>(n_rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+  cuuint32_t box[2] = {row_bytes / 8, 1};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SPECDEC_ERR_INVALID, "cuTensorMapEncodeTiled (rows) failed (%d)", static_cast<int>(r));
+  return SPECDEC_OK;
+}
+
 // Query positions per work item: rows (n_rep x positions) must fit the verify
 // kernel's row tile of 32 (TMEM columns of S and O).
 static int q_tile_for(int n_rep, int D) {
@@ -587,7 +605,7 @@ static int launch_verify(const AttnParams& p, const CUtensorMap& kmap, const CUt
   set_smem_attr(verify_kernel<NR, VF8, TMAP, D>, Geo::SMEM, attr);
   // persistent: one CTA per SM, the plan's C = target_items / 4 ranges
   const int grid = p.target_items / 4;
-  return launch_k("verify_kernel", verify_kernel<NR, VF8, TMAP, D>, dim3(grid), dim3(kV3Threads), Geo::SMEM, st,
+  return launch_k("verify_kernel", verify_kernel<NR, VF8, TMAP, D>, dim3(grid), dim3(v3_threads<VF8>()), Geo::SMEM, st,
                   pdl, p, kmap, vmap);
 }
 
@@ -893,4 +911,49 @@ extern "C" int specdec_attention(const void* q, const void* k, const void* v, vo
   if (int rc = encode_kv_map(&vmap, v, B * KV, T, D)) return rc;
   if (D == 128) return run_attention<128, false, true>(p, kmap, vmap, true, st);
   return run_attention<64, false, true>(p, kmap, vmap, true, st);
+}
+
+// ---------------------------------------------------------------- gather4 self-check
+// One CTA loads rows r[0..3] of a [n_rows][2048 B] tensor and of a [n_rows][64 B]
+// tensor with one tile::gather4 request each (the page-row loads of the attention
+// kernel) and writes the 8192 + 256 bytes it received to `out`.
+namespace sd {
+__global__ void __launch_bounds__(128) gather4_selftest_kernel(const __grid_constant__ CUtensorMap big,
+                                                               const __grid_constant__ CUtensorMap small, int4 rows,
+                                                               uint8_t* out, int32_t* status) {
+  __shared__ __align__(1024) uint8_t buf[8192 + 256];
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&bar, 8192 + 256);
+    tma_gather4(buf, &big, 0, rows.x, rows.y, rows.z, rows.w, &bar);
+    tma_gather4(buf + 8192, &small, 0, rows.x, rows.y, rows.z, rows.w, &bar);
+  }
+  const bool ok = __all_sync(0xffffffffu, mbar_wait(&bar, 0));
+  if (!ok) {
+    if (threadIdx.x == 0) raise_status(status, SPECDEC_STATUS_TIMEOUT);
+    return;
+  }
+  for (int i = threadIdx.x; i < (8192 + 256) / 16; i += blockDim.x)
+    reinterpret_cast<uint4*>(out)[i] = reinterpret_cast<const uint4*>(buf)[i];
+}
+}  // namespace sd
+
+extern "C" int specdec_gather4_selftest(const void* big, const void* small, int64_t n_rows, const int32_t* rows,
+                                        void* out, int32_t* status, specdec_stream_t stream) {
+  if (!big || !small || !rows || !out || n_rows <= 0) return fail(SPECDEC_ERR_INVALID, "bad gather4 self-test arguments");
+  for (int i = 0; i < 4; ++i)
+    if (rows[i] < 0 || rows[i] >= n_rows) return fail(SPECDEC_ERR_INVALID, "gather4 self-test row out of range");
+  if ((reinterpret_cast<uintptr_t>(big) | reinterpret_cast<uintptr_t>(small)) & 15u)
+    return fail(SPECDEC_ERR_INVALID, "gather4 self-test tensors must be 16-byte aligned");
+  CUtensorMap mb, ms;
+  if (int rc = encode_rows_map(&mb, big, static_cast<uint64_t>(n_rows), 2048)) return rc;
+  if (int rc = encode_rows_map(&ms, small, static_cast<uint64_t>(n_rows), 64)) return rc;
+  sd::gather4_selftest_kernel<<<1, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      mb, ms, make_int4(rows[0], rows[1], rows[2], rows[3]), static_cast<uint8_t*>(out), status);
+  return after_launch("gather4_selftest_kernel");
 }

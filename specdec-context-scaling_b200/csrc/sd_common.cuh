@@ -103,6 +103,17 @@ SD_DEV void tma_load_3d(void* dst, const CUtensorMap* map, int32_t c0, int32_t c
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
       : "memory");
 }
+// Four rows of a 2-D tensor map in one request (tile::gather4): rows r0 .. r3 starting
+// at element x (the map's box is one row high), written to dst as four consecutive
+// rows; completion is counted on the mbarrier.
+SD_DEV void tma_gather4(void* dst, const CUtensorMap* map, int32_t x, int32_t r0, int32_t r1, int32_t r2, int32_t r3,
+                        uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
+      : "memory");
+}
 SD_DEV void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

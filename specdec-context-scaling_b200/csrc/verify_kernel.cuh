@@ -2,7 +2,7 @@
 // tensor cores (tcgen05, TMEM accumulators) for head_dim 128.  Included inside
 // namespace sd by paged_attention.cu, after split_kernel.cuh.
 //
-// Persistent CTAs (one per SM) over a balanced page range, 320 threads:
+// Persistent CTAs (one per SM) over a balanced page range, 320 threads (448 for E4M3 V):
 //   warps 0-7  softmax + epilogue; warp w owns keys 32 (w % 4) .. +31 of each
 //              128-key tile (TMEM lane quarter w % 4) for the query rows of half
 //              w / 4, and in the epilogue output dims 32 (w % 4) .. +31 of those rows
@@ -11,6 +11,8 @@
 //              image of the pool; V likewise, or raw E4M3 rows + per-token scales),
 //              and the Q rows of each item
 //   warp 9     MMA issuer (one lane) and owner of the TMEM allocation
+//   warps 10-13 (E4M3 V only) converters: widen each tile's E4M3 rows to f16 in
+//              shared memory while the softmax warps work on the same tile
 // Per tile t (buffer b = t & 1):
 //   S^T[b] (128 keys x NR rows, fp32, TMEM)  = K_tile . Q^T            (8 x K=16 MMAs)
 //   softmax warps: row maxima over the tile, lazy online rescale of O (only when a
@@ -25,7 +27,11 @@
 constexpr int kSmWarps = 8;                    // softmax warps: (key quarter, row half)
 constexpr int kProducerWarp = kSmWarps;        // bulk-TMA producer
 constexpr int kMmaWarp = kSmWarps + 1;         // MMA issuer, TMEM owner
-constexpr int kV3Threads = 32 * (kSmWarps + 2);
+constexpr int kCvtWarp0 = kSmWarps + 2;        // E4M3 V: first of kCvtWarps converter warps
+constexpr int kCvtWarps = 4;
+// threads of one CTA: softmax, producer, MMA (+ converters for E4M3 V)
+template <bool VF8>
+constexpr int v3_threads() { return 32 * (kSmWarps + 2 + (VF8 ? kCvtWarps : 0)); }
 constexpr int kTileKeys = 128;
 constexpr int kTilePages = 8;
 constexpr float kRescaleLog2 = 8.f;   // lazy rescale threshold (log2 units)

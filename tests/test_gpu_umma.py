@@ -27,3 +27,28 @@ def test_umma_selftest_matches_matmul():
     assert int(st.item()) == 0
     torch.testing.assert_close(o1.cpu(), k.float() @ q.float().T, rtol=1e-5, atol=1e-3)
     torch.testing.assert_close(o2.cpu(), v.float().T @ p.float().T, rtol=1e-5, atol=1e-3)
+
+
+def test_tma_gather4_page_rows():
+    """Four-row tensor gathers (one-row boxes) fetch exactly the requested 2048-byte and
+    64-byte rows: the page-row loads of the attention kernel."""
+    import ctypes
+
+    from specdec_b200 import _lib
+
+    lib = _lib.load_library()
+    n = 1000
+    g = torch.Generator().manual_seed(3)
+    big = torch.randint(0, 256, (n, 2048), generator=g, dtype=torch.uint8).cuda()
+    small = torch.randint(0, 256, (n, 64), generator=g, dtype=torch.uint8).cuda()
+    for rows in ([7, 0, 999, 7], [500, 501, 2, 3]):
+        out = torch.zeros(8192 + 256, dtype=torch.uint8, device="cuda")
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        r = (ctypes.c_int32 * 4)(*rows)
+        rc = lib.specdec_gather4_selftest(big.data_ptr(), small.data_ptr(), n, ctypes.cast(r, ctypes.c_void_p),
+                                          out.data_ptr(), status.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        assert rc == 0, _lib.status_message(rc) if hasattr(_lib, "status_message") else rc
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        assert torch.equal(out[:8192].view(4, 2048).cpu(), big[rows].cpu())
+        assert torch.equal(out[8192:].view(4, 64).cpu(), small[rows].cpu())
