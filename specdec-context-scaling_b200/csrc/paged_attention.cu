@@ -598,7 +598,8 @@ static int launch_k(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 bl
 }
 
 template <int NR, bool VF8, bool TMAP, int D>
-static int launch_verify(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, cudaStream_t st,
+static int launch_verify(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                         const CUtensorMap& smap, cudaStream_t st,
                          bool pdl) {
   using Geo = V3Geom<NR, VF8, D>;
   static bool attr[64] = {};
@@ -606,7 +607,7 @@ static int launch_verify(const AttnParams& p, const CUtensorMap& kmap, const CUt
   // persistent: one CTA per SM, the plan's C = target_items / 4 ranges
   const int grid = p.target_items / 4;
   return launch_k("verify_kernel", verify_kernel<NR, VF8, TMAP, D>, dim3(grid), dim3(v3_threads<VF8>()), Geo::SMEM, st,
-                  pdl, p, kmap, vmap);
+                  pdl, p, kmap, vmap, smap);
 }
 
 // CTAs of the persistent verify kernel: the caller's SM budget, at most the device's
@@ -637,7 +638,8 @@ static int record_event(void* ev, cudaStream_t stream) {
 }
 
 template <int D, bool VF8, bool TMAP>
-static int run_attention(AttnParams p, const CUtensorMap& kmap, const CUtensorMap& vmap, bool build_plan,
+static int run_attention(AttnParams p, const CUtensorMap& kmap, const CUtensorMap& vmap, const CUtensorMap& smap,
+                         bool build_plan,
                          cudaStream_t stream, void* ev_begin = nullptr, void* ev_end = nullptr) {
   if (build_plan) {
     plan_kernel<<<1, 1024, 0, stream>>>(p);
@@ -648,8 +650,8 @@ static int run_attention(AttnParams p, const CUtensorMap& kmap, const CUtensorMa
   // profiling events between the kernels need ordinary launches
   const bool pdl = ev_begin == nullptr && ev_end == nullptr;
   const int rows_max = p.n_rep * (p.q_tile < p.max_q_len ? p.q_tile : p.max_q_len);
-  const int rc = rows_max <= 16 ? launch_verify<16, VF8, TMAP, D>(p, kmap, vmap, stream, pdl)
-                                : launch_verify<32, VF8, TMAP, D>(p, kmap, vmap, stream, pdl);
+  const int rc = rows_max <= 16 ? launch_verify<16, VF8, TMAP, D>(p, kmap, vmap, smap, stream, pdl)
+                                : launch_verify<32, VF8, TMAP, D>(p, kmap, vmap, smap, stream, pdl);
   if (rc) return rc;
   return record_event(ev_end, stream);
 }
@@ -755,8 +757,18 @@ static int paged_entry(const SpecdecAttnArgs* a, cudaStream_t stream, bool plan_
     plan_kernel<<<1, 1024, 0, stream>>>(p);
     return after_launch("plan_kernel");
   }
-  CUtensorMap dummy;
-  memset(&dummy, 0, sizeof(dummy));
+  // page-row maps over the pools for the kernel's four-row gathers: K (and bf16 V) as
+  // rows of 128 bytes x 16 tokens = one dim half of a page-head block, E4M3 V as one
+  // 2048-byte row per page-head block, scales as one 64-byte row
+  const int KH = D / 64;
+  const uint64_t blocks = static_cast<uint64_t>(a->kv.num_pages) * a->kv.num_kv_heads;
+  CUtensorMap kmap, vmap, smap;
+  memset(&smap, 0, sizeof(smap));
+  if (int rc = encode_rows_map(&kmap, a->kv.k_pool, blocks * KH, 2048)) return rc;
+  if (int rc = encode_rows_map(&vmap, a->kv.v_pool, vf8 ? blocks : blocks * KH, 2048)) return rc;
+  if (vf8) {
+    if (int rc = encode_rows_map(&smap, a->kv.v_scale, blocks, 64)) return rc;
+  }
   const bool build = a->reuse_plan == 0;
   // early loads need a plan from an earlier call (one built now is written by the
   // kernel right before) and the caller's promise about the history
@@ -764,10 +776,10 @@ static int paged_entry(const SpecdecAttnArgs* a, cudaStream_t stream, bool plan_
   void* eb = a->split_event_begin;
   void* ee = a->split_event_end;
   if (D == 128) {
-    return vf8 ? run_attention<128, true, false>(p, dummy, dummy, build, stream, eb, ee)
-               : run_attention<128, false, false>(p, dummy, dummy, build, stream, eb, ee);
+    return vf8 ? run_attention<128, true, false>(p, kmap, vmap, smap, build, stream, eb, ee)
+               : run_attention<128, false, false>(p, kmap, vmap, smap, build, stream, eb, ee);
   }
-  return run_attention<64, false, false>(p, dummy, dummy, build, stream, eb, ee);
+  return run_attention<64, false, false>(p, kmap, vmap, smap, build, stream, eb, ee);
 }
 
 }  // namespace sd
@@ -909,8 +921,10 @@ extern "C" int specdec_attention(const void* q, const void* k, const void* v, vo
   CUtensorMap kmap, vmap;
   if (int rc = encode_kv_map(&kmap, k, B * KV, T, D)) return rc;
   if (int rc = encode_kv_map(&vmap, v, B * KV, T, D)) return rc;
-  if (D == 128) return run_attention<128, false, true>(p, kmap, vmap, true, st);
-  return run_attention<64, false, true>(p, kmap, vmap, true, st);
+  CUtensorMap smap;
+  memset(&smap, 0, sizeof(smap));
+  if (D == 128) return run_attention<128, false, true>(p, kmap, vmap, smap, true, st);
+  return run_attention<64, false, true>(p, kmap, vmap, smap, true, st);
 }
 
 // ---------------------------------------------------------------- gather4 self-check
