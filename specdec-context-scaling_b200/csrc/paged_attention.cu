@@ -57,6 +57,8 @@ struct PlanHeader {
 static_assert(sizeof(PlanHeader) == 256, "plan header is 256 bytes");
 
 constexpr int kMaxRows = 64;  // query rows (n_rep x query positions) per work item
+// per split item and row: the row max (log2 units) and four key-quarter partial sums
+constexpr int kStatRows = 5;
 constexpr int kMergeWide = 16;  // groups with at least this many splits are merged by whole CTAs
 
 struct WsLayout {
@@ -73,7 +75,7 @@ static WsLayout ws_layout(int B, int KV, int max_qtiles, int D, int target_items
   w.ctas = align_up(w.groups + sizeof(GroupInfo) * (size_t)w.max_groups, 256);
   w.mlist = align_up(w.ctas + sizeof(int32_t) * (size_t)(target_items / 4 + 1), 256);
   w.lse = align_up(w.mlist + sizeof(GroupInfo) * (size_t)w.max_groups, 256);
-  w.po = align_up(w.lse + sizeof(float) * kMaxRows * (size_t)w.max_items, 256);
+  w.po = align_up(w.lse + sizeof(float) * kStatRows * kMaxRows * (size_t)w.max_items, 256);
   w.total = align_up(w.po + sizeof(float) * kMaxRows * (size_t)D * w.max_items, 256);
   return w;
 }
@@ -98,7 +100,7 @@ struct AttnParams {
   GroupInfo* groups;
   int32_t* cta_first;  // [C + 1]: items of persistent CTA c are cta_first[c] .. cta_first[c+1]-1
   GroupInfo* merge_list;  // [max_groups]: the groups with more than one split (see PlanHeader)
-  float* p_lse;
+  float* p_stat;  // [item][kStatRows][kMaxRows]: row max, then key-quarter sums
   float* p_o;
   int32_t max_items, max_groups, target_items;
   int32_t tile_pages;  // the verify kernel consumes keys in tiles of this many pages
@@ -291,28 +293,31 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
 
 // ---------------------------------------------------------------- split merge
 // Log-sum-exp merge of split partials, run by the verify kernel's CTAs once every
-// CTA has written its partials (after its grid barrier).  A unit is one query row
-// of a group in the plan's merge_list (the groups with more than one split).  Rows
-// of groups with >= kMergeWide splits are merged by a whole CTA (its warps take
-// every NWARP-th split and combine in shared memory); the other rows by one warp
-// each.  Lane l owns dims 4(l % NQ) .. +3 of the splits s = l / NQ (mod SPW), so
-// every lane streams float4 partial rows; the state is an online (max, sum, acc).
-// Partials come from other CTAs of the same launch, so they are read with
-// L1-bypassing loads.
+// CTA has written its partials (after its grid barrier).  A split item leaves, per
+// query row, its unnormalised O row (sum over its keys of p v, p = 2^(s - m)), its
+// row max m and four key-quarter partial sums of p; the merge rescales them to the
+// common max and normalises once.  A unit is one query row of a group in the plan's
+// merge_list (the groups with more than one split).  Rows of groups with >=
+// kMergeWide splits are merged by a whole CTA (its warps take every NWARP-th split
+// and combine in shared memory); the other rows by one warp each.  Lane l owns dims
+// 4(l % NQ) .. +3 of the splits s = l / NQ (mod SPW), so every lane streams float4
+// partial rows; the state is an online (max, sum, acc).  Partials come from other
+// CTAs of the same launch, so they are read with L1-bypassing loads.
 struct MergeState {
   float m, l;
   float4 a;
 };
-SD_DEV void merge_absorb(MergeState& st, float lse, const float4& v) {
-  if (lse == -INFINITY) return;  // empty partial
-  const float m = fmaxf(st.m, lse);
+// absorb one split: its row max m, its sum L of p, its unnormalised row v
+SD_DEV void merge_absorb(MergeState& st, float m_s, float L_s, const float4& v) {
+  if (m_s == -INFINITY) return;  // the split sees no key of this row
+  const float m = fmaxf(st.m, m_s);
   const float f = (st.m == -INFINITY) ? 0.f : fast_exp2(st.m - m);
-  const float w = fast_exp2(lse - m);
+  const float w = fast_exp2(m_s - m);
   st.a.x = st.a.x * f + v.x * w;
   st.a.y = st.a.y * f + v.y * w;
   st.a.z = st.a.z * f + v.z * w;
   st.a.w = st.a.w * f + v.w * w;
-  st.l = st.l * f + w;
+  st.l = st.l * f + L_s * w;
   st.m = m;
 }
 SD_DEV void merge_combine(MergeState& st, const MergeState& o) {
@@ -328,36 +333,43 @@ SD_DEV void merge_combine(MergeState& st, const MergeState& o) {
   st.m = m;
 }
 
-// s_st: NWARP x 32 states of shared memory (the caller's free staging area)
+// s_st: NWARP x 32 states of shared memory (the caller's free staging area).
+// n_wide / n_narrow: the plan's merge-list counts; pre_w / pre_n: the merge-list
+// entries of this CTA's first wide unit and this warp's first narrow unit, loaded
+// before the grid barrier.
 template <int D, int NWARP>
-SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int warp, int lane) {
+SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int warp, int lane, int n_wide, int n_narrow,
+                         const GroupInfo& pre_w, const GroupInfo& pre_n) {
   constexpr int NQ = D / 4;     // dim quads
   constexpr int SPW = 32 / NQ;  // split slots per warp
   const int quad = lane % NQ, slot = lane / NQ;
   const int RU = p.n_rep * min(p.q_tile, p.max_q_len);  // row slots per group
-  const int wide_units = p.hdr->num_merge_wide * RU;
-  const int narrow_units = p.hdr->num_merge_narrow * RU;
+  const int wide_units = n_wide * RU;
+  const int narrow_units = n_narrow * RU;
 
   // the splits s = s0, s0 + step, ... of row r of group grp
   auto stream = [&](const GroupInfo& grp, int r, int s0, int step, MergeState& st) {
     st.m = -INFINITY;
     st.l = 0.f;
     st.a = make_float4(0.f, 0.f, 0.f, 0.f);
-    const int64_t base = static_cast<int64_t>(grp.first_item) * kMaxRows + r;
     for (int s = s0; s < grp.nsplit; s += 8 * step) {
-      float lse[8];
+      float ms[8], ls[8];
       float4 v[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const int sk = s + k * step;
         const bool in = sk < grp.nsplit;
-        lse[k] = in ? __ldcg(p.p_lse + base + static_cast<int64_t>(sk) * kMaxRows) : -INFINITY;
-        v[k] = in ? __ldcg(reinterpret_cast<const float4*>(p.p_o + (base + static_cast<int64_t>(sk) * kMaxRows) * D) +
-                           quad)
+        const int64_t item = static_cast<int64_t>(grp.first_item) + sk;
+        const float* st_row = p.p_stat + item * (kStatRows * kMaxRows) + r;
+        ms[k] = in ? __ldcg(st_row) : -INFINITY;
+        ls[k] = in ? (__ldcg(st_row + kMaxRows) + __ldcg(st_row + 2 * kMaxRows)) +
+                         (__ldcg(st_row + 3 * kMaxRows) + __ldcg(st_row + 4 * kMaxRows))
+                   : 0.f;
+        v[k] = in ? __ldcg(reinterpret_cast<const float4*>(p.p_o + (item * kMaxRows + r) * D) + quad)
                   : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
-      for (int k = 0; k < 8; ++k) merge_absorb(st, lse[k], v[k]);
+      for (int k = 0; k < 8; ++k) merge_absorb(st, ms[k], ls[k], v[k]);
     }
   };
   auto finish = [&](const GroupInfo& grp, int r, MergeState st) {
@@ -385,7 +397,7 @@ SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int warp, int la
 
   // wide rows: one CTA each
   for (int u = blockIdx.x; u < wide_units; u += gridDim.x) {
-    const GroupInfo grp = p.merge_list[u / RU];
+    const GroupInfo grp = u == static_cast<int>(blockIdx.x) ? pre_w : p.merge_list[u / RU];
     const int r = u % RU;
     if (r >= p.n_rep * grp.nq) continue;  // uniform per CTA
     MergeState st;
@@ -400,8 +412,9 @@ SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int warp, int la
     __syncthreads();
   }
   // narrow rows: one warp each
-  for (int u = blockIdx.x * NWARP + warp; u < narrow_units; u += gridDim.x * NWARP) {
-    const GroupInfo grp = p.merge_list[p.max_groups - 1 - u / RU];
+  const int u0 = blockIdx.x * NWARP + warp;
+  for (int u = u0; u < narrow_units; u += gridDim.x * NWARP) {
+    const GroupInfo grp = u == u0 ? pre_n : p.merge_list[p.max_groups - 1 - u / RU];
     const int r = u % RU;
     if (r >= p.n_rep * grp.nq) continue;  // uniform per warp
     MergeState st;
@@ -669,7 +682,7 @@ static int fill_workspace(AttnParams& p, void* ws, size_t ws_bytes, int B, int K
   p.groups = reinterpret_cast<GroupInfo*>(base + w.groups);
   p.cta_first = reinterpret_cast<int32_t*>(base + w.ctas);
   p.merge_list = reinterpret_cast<GroupInfo*>(base + w.mlist);
-  p.p_lse = reinterpret_cast<float*>(base + w.lse);
+  p.p_stat = reinterpret_cast<float*>(base + w.lse);
   p.p_o = reinterpret_cast<float*>(base + w.po);
   p.max_items = w.max_items;
   p.max_groups = w.max_groups;

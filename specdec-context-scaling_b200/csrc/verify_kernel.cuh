@@ -38,20 +38,22 @@ constexpr float kRescaleLog2 = 8.f;   // lazy rescale threshold (log2 units)
 constexpr float kScaleSlack = 16.f;   // lazy growth of the E4M3 reference scale
 
 // Shared-memory / TMEM plan of one CTA.  D = 128: K and V tiles are [2 dim halves]
-// [128 keys][128 B].  D = 64: one dim half; the V stage keeps a second, all-zero half
-// so the PV MMA runs with M = 128 (dims 64-127 of O^T stay zero and are never read).
+// [128 keys][128 B].  D = 64: one dim half.  The PV MMA still runs with M = 128: its
+// second 64-row half of V^T is the 16 KB that follow the stage (the next V stage, or
+// K stage 0 after the last one -- the V stages come first), which only feeds rows
+// 64-127 of O^T; those rows are never read.
 template <int NR, bool VF8, int D>
 struct V3Geom {
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
   static_assert(!VF8 || D == 128, "E4M3 V needs head_dim 128");
   static constexpr int KH = D / 64;                      // 128-byte dim halves of a K row
-  static constexpr int NS = VF8 ? 2 : (D == 128 ? 3 : 4);  // ring depth (tiles)
+  static constexpr int NS = VF8 ? 2 : (D == 128 ? 3 : 6);  // ring depth (tiles)
   static constexpr int KT = 16384 * KH;                  // K tile bytes
-  static constexpr int VT = VF8 ? 16384 : 32768;         // V tile bytes as staged (D 64: half 1 zero)
+  static constexpr int VT = VF8 ? 16384 : 16384 * KH;    // V tile bytes as staged
   static constexpr int ST = VF8 ? 512 : 0;               // 128 scales
-  static constexpr int K_OFF = 0;
-  static constexpr int V_OFF = K_OFF + NS * KT;
-  static constexpr int S_OFF = V_OFF + NS * VT;
+  static constexpr int V_OFF = D == 64 ? 0 : NS * KT;
+  static constexpr int K_OFF = D == 64 ? NS * VT : 0;
+  static constexpr int S_OFF = (D == 64 ? K_OFF + NS * KT : V_OFF + NS * VT);
   static constexpr int VC_OFF = ((S_OFF + NS * ST + 1023) / 1024) * 1024;  // widened V (E4M3 only)
   static constexpr int Q_OFF = VC_OFF + (VF8 ? 2 * 32768 : 0);
   static constexpr int QH = NR * 128;                    // one dim half of Q: [NR rows][128 B]
@@ -60,6 +62,7 @@ struct V3Geom {
   static constexpr int SMEM = P_OFF + 2 * QB + 1024;     // + alignment slack
   static constexpr int TMEM_COLS = NR <= 16 ? 64 : 128;  // S[2] + O = 3 NR columns
   static constexpr int PAGE_BYTES = 2048 * KH + (VF8 ? 2048 + 64 : 2048 * KH);  // bytes copied per page
+  static_assert(D == 128 || (V_OFF == 0 && K_OFF == NS * VT), "D 64: PV's upper half reads the next 16 KB");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
