@@ -307,19 +307,6 @@ struct MergeState {
   float m, l;
   float4 a;
 };
-// absorb one split: its row max m, its sum L of p, its unnormalised row v
-SD_DEV void merge_absorb(MergeState& st, float m_s, float L_s, const float4& v) {
-  if (m_s == -INFINITY) return;  // the split sees no key of this row
-  const float m = fmaxf(st.m, m_s);
-  const float f = (st.m == -INFINITY) ? 0.f : fast_exp2(st.m - m);
-  const float w = fast_exp2(m_s - m);
-  st.a.x = st.a.x * f + v.x * w;
-  st.a.y = st.a.y * f + v.y * w;
-  st.a.z = st.a.z * f + v.z * w;
-  st.a.w = st.a.w * f + v.w * w;
-  st.l = st.l * f + L_s * w;
-  st.m = m;
-}
 SD_DEV void merge_combine(MergeState& st, const MergeState& o) {
   if (o.m == -INFINITY) return;
   const float m = fmaxf(st.m, o.m);
@@ -368,8 +355,25 @@ SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int warp, int la
         v[k] = in ? __ldcg(reinterpret_cast<const float4*>(p.p_o + (item * kMaxRows + r) * D) + quad)
                   : make_float4(0.f, 0.f, 0.f, 0.f);
       }
+      // the batch's max first, so the eight weights are independent
+      float mb = ms[0];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) merge_absorb(st, ms[k], ls[k], v[k]);
+      for (int k = 1; k < 8; ++k) mb = fmaxf(mb, ms[k]);
+      if (mb == -INFINITY) continue;
+      MergeState bt;
+      bt.m = mb;
+      bt.l = 0.f;
+      bt.a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float w = fast_exp2(ms[k] - mb);  // 0 for an empty split (-inf)
+        bt.a.x += v[k].x * w;
+        bt.a.y += v[k].y * w;
+        bt.a.z += v[k].z * w;
+        bt.a.w += v[k].w * w;
+        bt.l += ls[k] * w;
+      }
+      merge_combine(st, bt);
     }
   };
   auto finish = [&](const GroupInfo& grp, int r, MergeState st) {
@@ -405,8 +409,27 @@ SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int warp, int la
     s_st[warp * 32 + lane] = st;
     __syncthreads();
     if (warp == 0) {
-#pragma unroll 1
-      for (int w = 1; w < NWARP; ++w) merge_combine(st, s_st[w * 32 + lane]);
+      // the warps' states: common max first, then independent weights
+      float m = st.m;
+#pragma unroll
+      for (int w = 1; w < NWARP; ++w) m = fmaxf(m, s_st[w * 32 + lane].m);
+      if (m != -INFINITY) {
+        MergeState tot;
+        tot.m = m;
+        tot.l = 0.f;
+        tot.a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < NWARP; ++w) {
+          const MergeState o = s_st[w * 32 + lane];
+          const float g = fast_exp2(o.m - m);  // 0 for an empty state (-inf)
+          tot.a.x += o.a.x * g;
+          tot.a.y += o.a.y * g;
+          tot.a.z += o.a.z * g;
+          tot.a.w += o.a.w * g;
+          tot.l += o.l * g;
+        }
+        st = tot;
+      }
       finish(grp, r, st);
     }
     __syncthreads();
