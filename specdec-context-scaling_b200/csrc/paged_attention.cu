@@ -637,7 +637,7 @@ template <int NR, bool VF8, bool TMAP, int D>
 static int launch_verify(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
                          const CUtensorMap& smap, cudaStream_t st,
                          bool pdl) {
-  using Geo = V3Geom<NR, VF8, D>;
+  using Geo = V3Geom<NR == 8 ? 16 : NR, VF8, D>;
   static bool attr[64] = {};
   set_smem_attr(verify_kernel<NR, VF8, TMAP, D>, Geo::SMEM, attr);
   // persistent: one CTA per SM, the plan's C = target_items / 4 ranges
@@ -686,8 +686,9 @@ static int run_attention(AttnParams p, const CUtensorMap& kmap, const CUtensorMa
   // profiling events between the kernels need ordinary launches
   const bool pdl = ev_begin == nullptr && ev_end == nullptr;
   const int rows_max = p.n_rep * (p.q_tile < p.max_q_len ? p.q_tile : p.max_q_len);
-  const int rc = rows_max <= 16 ? launch_verify<16, VF8, TMAP, D>(p, kmap, vmap, smap, stream, pdl)
-                                : launch_verify<32, VF8, TMAP, D>(p, kmap, vmap, smap, stream, pdl);
+  const int rc = rows_max <= 8    ? launch_verify<8, VF8, TMAP, D>(p, kmap, vmap, smap, stream, pdl)
+                 : rows_max <= 16 ? launch_verify<16, VF8, TMAP, D>(p, kmap, vmap, smap, stream, pdl)
+                                  : launch_verify<32, VF8, TMAP, D>(p, kmap, vmap, smap, stream, pdl);
   if (rc) return rc;
   return record_event(ev_end, stream);
 }

@@ -90,6 +90,17 @@ def test_ragged_batch_mixed_rows(fp8):
     assert_close_attention(got, ref, f"ragged fp8={fp8}")
 
 
+@pytest.mark.parametrize("fp8,H,D", [(False, 12, 128), (True, 12, 128), (False, 14, 64), (False, 16, 128)])
+def test_ragged_decode_rows(fp8, H, D):
+    """Decode-only batches (at most 8 query rows per item: two warp groups on alternate
+    tiles): one-tile items, CTAs with several items, direct and split items."""
+    rng = torch.Generator().manual_seed(11 + H + D)
+    lens = [int(x) for x in torch.randint(1, 5000, (40,), generator=rng)] + [1, 16, 17, 128, 129, 8192]
+    q_lens = [1] * len(lens)
+    got, ref, *_ = _paged_case(lens, q_lens, H, 2, D, fp8, seed=21)
+    assert_close_attention(got, ref, f"decode rows fp8={fp8} H={H} D={D}")
+
+
 def test_plan_reuse_across_layers():
     """One plan serves every layer: reuse_plan=True gives the same output as a fresh plan."""
     ops = _ops()
