@@ -21,6 +21,9 @@
  *                                   whole-history V dequantisation, kv_repeat, masked softmax)
  *   specdec_append_kv            <- quantize_kv_fp8(v, GROUP_V) + cache append,
  *                                   specdec/engine/model_self.py:304-314 and :778-800
+ *   specdec_rope_append          <- apply_rope of q and k (specdec/engine/model_self.py:286-296)
+ *                                   followed by the cache append above, in one launch
+ *   specdec_swiglu_packed        <- swiglu_cuda over a fused gate|up projection
  *   specdec_greedy_accept        <- vectorised accept, experiments/execution_optimization/
  *                                   fast_spec_dec.py:246-256 (strict form spec_dec.py:230-250)
  *   specdec_trim                 <- spec_cache.trim_cache, specdec/engine/spec_cache.py:10-28
@@ -200,6 +203,29 @@ typedef struct SpecdecAppendArgs {
 int specdec_append_kv(const SpecdecAppendArgs* args, specdec_stream_t stream);
 
 /*
+ * Fused rotary embedding + KV append of one decode / verify step (engine seam
+ * after the fused QKV projection; the reference applies apply_rope to q and k
+ * (specdec/engine/model_self.py:286-296) and then writes the cache).  qkv holds
+ * `rows` packed rows of (num_q_heads + 2 num_kv_heads) heads x head_dim bf16 values
+ * (q heads, k heads, v heads); cos / sin are (rows, head_dim) bf16 at each row's
+ * position.  q_out (rows, num_q_heads, head_dim) receives the rotated queries; the
+ * rotated k rows and the v rows of every sequence's first n_new[b] rows go to the
+ * pool exactly as specdec_append_kv writes them (kv.k_new, kv.v_new and the strides
+ * are unused).  Rounding: bf16(bf16(x cos) + bf16(rotate_half(x) sin)).
+ */
+typedef struct SpecdecRopeAppendArgs {
+  const void* qkv;
+  int64_t qkv_row_stride; /* elements */
+  const void* cos;
+  const void* sin;
+  void* q_out;
+  int32_t rows, num_q_heads;
+  SpecdecAppendArgs kv;
+} SpecdecRopeAppendArgs;
+
+int specdec_rope_append(const SpecdecRopeAppendArgs* args, specdec_stream_t stream);
+
+/*
  * Greedy accept on the device.  For sequence b, rows j = 0 .. n_rows[b]-1 of
  * logits (row (row0[b] + j), row stride `row_stride` elements, `vocab` columns)
  * give g[b][j] = argmax (first index on ties, NaN counts as the maximum, as
@@ -262,6 +288,9 @@ int specdec_apply_rope(const void* x, int64_t stride_b, int64_t stride_h, int64_
 /* out = silu(gate) * up, elementwise. */
 int specdec_swiglu(const void* gate, const void* up, void* out, int32_t dtype, int64_t n,
                    specdec_stream_t stream);
+/* SwiGLU of a fused gate|up projection (rows, 2 inter) bf16 -> (rows, inter), the
+ * rounding of specdec_swiglu; inter % 8 == 0, 16-byte aligned rows. */
+int specdec_swiglu_packed(const void* gate_up, void* out, int64_t rows, int64_t inter, specdec_stream_t stream);
 
 /* Diagnostics. */
 /* Tensor-core self-check (no counterpart in the reference): one CTA computes, with

@@ -99,9 +99,49 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const T* __restrict__ g, co
   }
 }
 
+// SwiGLU of a fused gate|up projection: row r of `gu` holds gate (inter values) then
+// up (inter values); 8 values per thread with 16-byte vectors (inter % 8 == 0).
+__global__ void __launch_bounds__(256) swiglu_packed_kernel(const __nv_bfloat16* __restrict__ gu,
+                                                            __nv_bfloat16* __restrict__ y, int64_t rows,
+                                                            int64_t inter) {
+  const int64_t n8 = rows * (inter / 8);
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / (inter / 8), c = (i - r * (inter / 8)) * 8;
+    const uint4 gv = *reinterpret_cast<const uint4*>(gu + r * 2 * inter + c);
+    const uint4 uv = *reinterpret_cast<const uint4*>(gu + r * 2 * inter + inter + c);
+    const __nv_bfloat16* g8 = reinterpret_cast<const __nv_bfloat16*>(&gv);
+    const __nv_bfloat16* u8 = reinterpret_cast<const __nv_bfloat16*>(&uv);
+    uint4 ov;
+    __nv_bfloat16* o8 = reinterpret_cast<__nv_bfloat16*>(&ov);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float g = __bfloat162float(g8[e]);
+      const float silu = round_to<__nv_bfloat16>(g / (1.f + expf(-g)));
+      o8[e] = __float2bfloat16_rn(silu * __bfloat162float(u8[e]));
+    }
+    *reinterpret_cast<uint4*>(y + r * inter + c) = ov;
+  }
+}
+
 }  // namespace sd
 
 using namespace sd;
+
+extern "C" int specdec_swiglu_packed(const void* gate_up, void* out, int64_t rows, int64_t inter,
+                                     specdec_stream_t stream) {
+  if (!gate_up || !out) return fail(SPECDEC_ERR_INVALID, "tensors must be CUDA");
+  if (rows < 0 || inter <= 0 || inter % 8 != 0) return fail(SPECDEC_ERR_INVALID, "rows >= 0 and inter % 8 == 0 required");
+  if ((reinterpret_cast<uintptr_t>(gate_up) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    return fail(SPECDEC_ERR_INVALID, "gate_up and out must be 16-byte aligned");
+  const int64_t n8 = rows * (inter / 8);
+  if (n8 == 0) return SPECDEC_OK;
+  int64_t blocks = (n8 + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  swiglu_packed_kernel<<<static_cast<unsigned>(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(gate_up), static_cast<__nv_bfloat16*>(out), rows, inter);
+  return after_launch("swiglu_packed_kernel");
+}
 
 extern "C" int specdec_rmsnorm(const void* x, const void* weight, void* out, int32_t dtype, int64_t rows,
                                int32_t hidden, float eps, specdec_stream_t stream) {

@@ -118,6 +118,19 @@ class AppendArgs(ctypes.Structure):
     ]
 
 
+class RopeAppendArgs(ctypes.Structure):
+    _fields_ = [
+        ("qkv", _vp),
+        ("qkv_row_stride", _i64),
+        ("cos", _vp),
+        ("sin", _vp),
+        ("q_out", _vp),
+        ("rows", _i32),
+        ("num_q_heads", _i32),
+        ("kv", AppendArgs),
+    ]
+
+
 class AcceptArgs(ctypes.Structure):
     _fields_ = [
         ("logits", _vp),
@@ -150,6 +163,7 @@ SIGNATURES = {
     "specdec_paged_attention": (ctypes.c_int, [ctypes.POINTER(AttnArgs), _vp]),
     "specdec_paged_attention_noalloc": (ctypes.c_int, [ctypes.POINTER(AttnArgs), _vp]),
     "specdec_append_kv": (ctypes.c_int, [ctypes.POINTER(AppendArgs), _vp]),
+    "specdec_rope_append": (ctypes.c_int, [ctypes.POINTER(RopeAppendArgs), _vp]),
     "specdec_accept_workspace_bytes": (_sz, [_i32, _i32, _i32]),
     "specdec_greedy_accept": (ctypes.c_int, [ctypes.POINTER(AcceptArgs), _vp]),
     "specdec_trim": (ctypes.c_int, [_vp, _vp, _vp, _i32, _vp, _vp]),
@@ -164,6 +178,7 @@ SIGNATURES = {
         [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp],
     ),
     "specdec_swiglu": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i64, _vp]),
+    "specdec_swiglu_packed": (ctypes.c_int, [_vp, _vp, _i64, _i64, _vp]),
     "specdec_umma_selftest": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "specdec_gather4_selftest": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp]),
     "specdec_last_error": (ctypes.c_char_p, []),

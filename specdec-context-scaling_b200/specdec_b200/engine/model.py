@@ -85,8 +85,7 @@ class _Layer:
     w_qkv: torch.Tensor
     b_qkv: torch.Tensor | None
     w_o: torch.Tensor
-    w_gate: torch.Tensor
-    w_up: torch.Tensor
+    w_gu: torch.Tensor  # gate_proj and up_proj stacked: (2 inter, hidden)
     w_down: torch.Tensor
     ln1: torch.Tensor
     ln2: torch.Tensor
@@ -147,8 +146,9 @@ class PagedModel:
             if (a + "q_proj.bias") in state:
                 b_qkv = torch.cat([get(a + "q_proj.bias"), get(a + "k_proj.bias"), get(a + "v_proj.bias")])
             self.layers.append(_Layer(w_qkv.contiguous(), None if b_qkv is None else b_qkv.contiguous(),
-                                      get(a + "o_proj.weight"), get(p + "mlp.gate_proj.weight"),
-                                      get(p + "mlp.up_proj.weight"), get(p + "mlp.down_proj.weight"),
+                                      get(a + "o_proj.weight"),
+                                      torch.cat([get(p + "mlp.gate_proj.weight"), get(p + "mlp.up_proj.weight")]),
+                                      get(p + "mlp.down_proj.weight"),
                                       get(p + "input_layernorm.weight"), get(p + "post_attention_layernorm.weight")))
         self.inv_freq = 1.0 / (cfg.rope_theta ** (torch.arange(0, cfg.head_dim, 2, device=self.device,
                                                                dtype=torch.float32) / cfg.head_dim))
@@ -182,8 +182,10 @@ class PagedModel:
         return q, k, v
 
     def _mlp(self, L: _Layer, x: torch.Tensor) -> torch.Tensor:
+        """x + down(silu(gate(h)) * up(h)), h = rmsnorm(x): one gate|up GEMM, the residual
+        added by the down GEMM (in place on x)."""
         h = ops.rmsnorm(x, L.ln2, self.cfg.eps)
-        return x + ops.swiglu(h @ L.w_gate.t(), h @ L.w_up.t()) @ L.w_down.t()
+        return x.addmm_(ops.swiglu_packed(h @ L.w_gu.t()), L.w_down.t())
 
     def logits(self, hidden_rows: torch.Tensor) -> torch.Tensor:
         """Tied LM head (model_self.py:857): (n, hidden) -> (n, vocab)."""
@@ -201,17 +203,22 @@ class PagedModel:
         rows = layout.rows
         x = self.embed[tokens.long()]
         cos, sin = self._cos_sin(layout.positions())
+        q = torch.empty(rows, c.heads, c.head_dim, dtype=x.dtype, device=x.device)
+        # attention writes every row of each sequence's q_len; padding rows stay unset
+        # (meaningless, never stored, never mixed into other rows)
+        o = torch.empty(rows, c.heads, c.head_dim, dtype=x.dtype, device=x.device)
         for li, L in enumerate(self.layers):
             h = ops.rmsnorm(x, L.ln1, c.eps)
-            q, k, v = self._qkv(L, h, cos, sin)
-            ops.append_kv(k[0].transpose(0, 1), v.transpose(0, 1), cache, li, row0=layout.q_row0,
-                          n_new=layout.q_len, pos0=layout.pos0, max_new=layout.q_max, status=status)
-            o = torch.zeros(rows, c.heads, c.head_dim, dtype=x.dtype, device=x.device)
+            qkv = torch.addmm(L.b_qkv, h, L.w_qkv.t()) if L.b_qkv is not None else h @ L.w_qkv.t()
+            # rotated q, and rotated k + v appended to the cache, in one launch
+            ops.rope_append(qkv.view(rows, c.heads + 2 * c.kv_heads, c.head_dim), cos, sin, cache, li,
+                            num_q_heads=c.heads, row0=layout.q_row0, n_new=layout.q_len, pos0=layout.pos0,
+                            max_new=layout.q_max, q_out=q, status=status)
             # layers after the first reuse layer 0's plan; the only KV the steps before write
             # is this step's new tokens, so the history may be loaded early
-            ops.paged_attention(q[0].transpose(0, 1), cache, li, layout.batch, out=o, workspace=workspace,
-                                reuse_plan=li > 0, status=status, history_ready=li > 0)
-            x = x + o.view(rows, c.heads * c.head_dim) @ L.w_o.t()
+            ops.paged_attention(q, cache, li, layout.batch, out=o, workspace=workspace, reuse_plan=li > 0,
+                                status=status, history_ready=li > 0)
+            x.addmm_(o.view(rows, c.heads * c.head_dim), L.w_o.t())
             x = self._mlp(L, x)
         return ops.rmsnorm(x, self.norm, c.eps)
 

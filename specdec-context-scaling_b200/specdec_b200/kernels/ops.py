@@ -331,12 +331,18 @@ def append_kv(k_new, v_new, cache: PagedKVCache, layer: int, *, row0, n_new, pos
             raise ValueError("k_new/v_new must be bf16 (rows, KV, D) with contiguous D")
     if k_new.stride() != v_new.stride():
         raise ValueError("k_new and v_new must share strides")
+    args = _append_args(cache, layer, row0, n_new, pos0, max_new, len_out, status, k_new.data_ptr(),
+                        v_new.data_ptr(), k_new.stride(0), k_new.stride(1))
+    _lib.check(_lib_handle().specdec_append_kv(ctypes.byref(args), _stream()), "append_kv")
+
+
+def _append_args(cache, layer, row0, n_new, pos0, max_new, len_out, status, k_ptr=0, v_ptr=0, st=0, sh=0):
     pool = cache.pools[layer]
-    args = _lib.AppendArgs(
-        k_new=k_new.data_ptr(),
-        v_new=v_new.data_ptr(),
-        stride_tok=k_new.stride(0),
-        stride_head=k_new.stride(1),
+    return _lib.AppendArgs(
+        k_new=k_ptr,
+        v_new=v_ptr,
+        stride_tok=st,
+        stride_head=sh,
         row0=row0.data_ptr(),
         n_new=n_new.data_ptr(),
         pos0=pos0.data_ptr(),
@@ -354,7 +360,39 @@ def append_kv(k_new, v_new, cache: PagedKVCache, layer: int, *, row0, n_new, pos
         max_pages_per_seq=cache.max_pages,
         status=_ptr(status),
     )
-    _lib.check(_lib_handle().specdec_append_kv(ctypes.byref(args), _stream()), "append_kv")
+
+
+def rope_append(qkv, cos, sin, cache: PagedKVCache, layer: int, *, num_q_heads: int, row0, n_new, pos0,
+                max_new: int, q_out=None, len_out=None, status=None):
+    """Rotate the q and k heads of a fused QKV projection ``qkv`` (rows, H + 2 KV, D) and append k / v.
+
+    Returns q_out (rows, H, D): the rotated queries.  The pool receives what
+    ``append_kv(apply_rope(k), v)`` would write, in one launch."""
+    if qkv.dtype != torch.bfloat16 or qkv.dim() != 3 or qkv.stride(2) != 1 or qkv.stride(1) != qkv.shape[2]:
+        raise ValueError("qkv must be bf16 (rows, heads, D) with contiguous heads")
+    rows, D = qkv.shape[0], qkv.shape[2]
+    for t in (cos, sin):
+        if t.dtype != torch.bfloat16 or t.shape != (rows, D) or not t.is_contiguous():
+            raise ValueError("cos/sin must be contiguous bf16 (rows, D)")
+    if q_out is None:
+        q_out = torch.empty(rows, num_q_heads, D, dtype=qkv.dtype, device=qkv.device)
+    args = _lib.RopeAppendArgs(qkv=qkv.data_ptr(), qkv_row_stride=qkv.stride(0), cos=cos.data_ptr(),
+                               sin=sin.data_ptr(), q_out=q_out.data_ptr(), rows=rows, num_q_heads=num_q_heads,
+                               kv=_append_args(cache, layer, row0, n_new, pos0, max_new, len_out, status))
+    _lib.check(_lib_handle().specdec_rope_append(ctypes.byref(args), _stream()), "rope_append")
+    return q_out
+
+
+def swiglu_packed(gate_up, out=None):
+    """silu(gate) * up of a fused (rows, 2 inter) bf16 projection -> (rows, inter)."""
+    if gate_up.dtype != torch.bfloat16 or gate_up.dim() != 2 or not gate_up.is_contiguous():
+        raise ValueError("gate_up must be contiguous bf16 (rows, 2 inter)")
+    rows, inter = gate_up.shape[0], gate_up.shape[1] // 2
+    if out is None:
+        out = torch.empty(rows, inter, dtype=gate_up.dtype, device=gate_up.device)
+    _lib.check(_lib_handle().specdec_swiglu_packed(gate_up.data_ptr(), out.data_ptr(), rows, inter, _stream()),
+               "swiglu_packed")
+    return out
 
 
 def accept_workspace(num_seqs: int, max_rows: int, vocab: int, device="cuda") -> torch.Tensor:

@@ -101,3 +101,41 @@ def test_gather_layer_round_trip():
                             cache.pools[0].v.cpu().view(torch.int16).numpy().view(np.uint16), None,
                             cache.page_table.cpu().numpy(), 0, 77)
     np.testing.assert_array_equal(k_np, u16(ks[0]))
+
+
+@pytest.mark.parametrize("fp8,H,D", [(True, 12, 128), (False, 12, 128), (False, 14, 64)])
+def test_rope_append_equals_rope_then_append(fp8, H, D):
+    """The fused step seam (one launch after the QKV projection) writes the same pool
+    bytes and rotated queries as apply_rope on q and k followed by append_kv."""
+    from specdec_b200.engine.paged_cache import PagedKVCache
+
+    ops = _ops()
+    KV, B, qmax = 2, 5, 5
+    before = [1, 13, 100, 16, 250]
+    q_len = [5, 1, 3, 5, 0]
+    rows = B * qmax
+    g = torch.Generator().manual_seed(31)
+    qkv = torch.randn(rows, H + 2 * KV, D, generator=g).to(torch.bfloat16).cuda()
+    cos = torch.randn(rows, D, generator=g).to(torch.bfloat16).cuda()
+    sin = torch.randn(rows, D, generator=g).to(torch.bfloat16).cuda()
+    row0 = torch.arange(B, dtype=torch.int32, device="cuda") * qmax
+    nn = torch.tensor(q_len, dtype=torch.int32, device="cuda")
+    pos0 = torch.tensor(before, dtype=torch.int32, device="cuda")
+    caches = [PagedKVCache.allocate(1, B, KV, D, 320, v_dtype="e4m3" if fp8 else "bf16", device="cuda",
+                                    page_order_seed=4) for _ in range(2)]
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    q_fused = ops.rope_append(qkv, cos, sin, caches[0], 0, num_q_heads=H, row0=row0, n_new=nn, pos0=pos0,
+                              max_new=qmax, status=status)
+    # unfused: rope of q and k as (1, heads, rows, D) views, then append
+    q_ref = ops.apply_rope(qkv[:, :H].transpose(0, 1).unsqueeze(0), cos, sin)[0].transpose(0, 1)
+    k_rot = ops.apply_rope(qkv[:, H:H + KV].transpose(0, 1).unsqueeze(0), cos, sin)[0].transpose(0, 1)
+    ops.append_kv(k_rot.contiguous(), qkv[:, H + KV:].contiguous(), caches[1], 0, row0=row0, n_new=nn, pos0=pos0,
+                  max_new=qmax, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert torch.equal(q_fused, q_ref)
+    a, b = caches[0].pools[0], caches[1].pools[0]
+    assert torch.equal(a.k.view(torch.int16), b.k.view(torch.int16))
+    assert torch.equal(a.v.view(torch.uint8), b.v.view(torch.uint8))
+    if fp8:
+        assert torch.equal(a.v_scale, b.v_scale)

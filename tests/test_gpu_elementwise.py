@@ -49,3 +49,11 @@ def test_swiglu():
     assert _bf16_ok(ops.swiglu(g.cuda(), u.cuda()), oel.swiglu(g, u))
     g32, u32 = g.float(), u.float()
     torch.testing.assert_close(ops.swiglu(g32.cuda(), u32.cuda()).cpu(), oel.swiglu(g32, u32), rtol=0, atol=1e-4)
+
+
+def test_swiglu_packed_equals_swiglu():
+    ops = _ops()
+    gu = torch.randn(33, 2 * 4864).to(torch.bfloat16).cuda()
+    got = ops.swiglu_packed(gu)
+    want = ops.swiglu(gu[:, :4864].contiguous(), gu[:, 4864:].contiguous())
+    assert torch.equal(got, want)
