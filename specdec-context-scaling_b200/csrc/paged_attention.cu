@@ -633,16 +633,16 @@ static int launch_k(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 bl
   return after_launch(what);
 }
 
-template <int NR, bool VF8, bool TMAP, int D>
+template <int NR, bool VF8, bool TMAP, int D, bool PP>
 static int launch_verify(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
                          const CUtensorMap& smap, cudaStream_t st,
                          bool pdl) {
-  using Geo = V3Geom<NR == 8 ? 16 : NR, VF8, D>;
+  using Geo = V3Geom<NR < 16 ? 16 : NR, VF8, D>;
   static bool attr[64] = {};
-  set_smem_attr(verify_kernel<NR, VF8, TMAP, D>, Geo::SMEM, attr);
+  set_smem_attr(verify_kernel<NR, VF8, TMAP, D, PP>, Geo::SMEM, attr);
   // persistent: one CTA per SM, the plan's C = target_items / 4 ranges
   const int grid = p.target_items / 4;
-  return launch_k("verify_kernel", verify_kernel<NR, VF8, TMAP, D>, dim3(grid), dim3(v3_threads<VF8>()), Geo::SMEM, st,
+  return launch_k("verify_kernel", verify_kernel<NR, VF8, TMAP, D, PP>, dim3(grid), dim3(v3_threads<VF8>()), Geo::SMEM, st,
                   pdl, p, kmap, vmap, smap);
 }
 
@@ -673,6 +673,11 @@ static int record_event(void* ev, cudaStream_t stream) {
   return SPECDEC_OK;
 }
 
+// softmax form per row class: two warp groups on alternate tiles (true) or one
+// group on every tile with the rows split in halves (false)
+constexpr bool kTwoGroup16 = true;
+constexpr bool kTwoGroup32 = false;
+
 template <int D, bool VF8, bool TMAP>
 static int run_attention(AttnParams p, const CUtensorMap& kmap, const CUtensorMap& vmap, const CUtensorMap& smap,
                          bool build_plan,
@@ -686,9 +691,9 @@ static int run_attention(AttnParams p, const CUtensorMap& kmap, const CUtensorMa
   // profiling events between the kernels need ordinary launches
   const bool pdl = ev_begin == nullptr && ev_end == nullptr;
   const int rows_max = p.n_rep * (p.q_tile < p.max_q_len ? p.q_tile : p.max_q_len);
-  const int rc = rows_max <= 8    ? launch_verify<8, VF8, TMAP, D>(p, kmap, vmap, smap, stream, pdl)
-                 : rows_max <= 16 ? launch_verify<16, VF8, TMAP, D>(p, kmap, vmap, smap, stream, pdl)
-                                  : launch_verify<32, VF8, TMAP, D>(p, kmap, vmap, smap, stream, pdl);
+  const int rc = rows_max <= 8    ? launch_verify<8, VF8, TMAP, D, true>(p, kmap, vmap, smap, stream, pdl)
+                 : rows_max <= 16 ? launch_verify<16, VF8, TMAP, D, kTwoGroup16>(p, kmap, vmap, smap, stream, pdl)
+                                  : launch_verify<32, VF8, TMAP, D, kTwoGroup32>(p, kmap, vmap, smap, stream, pdl);
   if (rc) return rc;
   return record_event(ev_end, stream);
 }

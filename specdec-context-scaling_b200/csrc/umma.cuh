@@ -128,6 +128,48 @@ SD_DEV void tmem_st8(uint32_t ta, const float (&v)[8]) {
                "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
                : "memory");
 }
+SD_DEV void tmem_ld4(uint32_t ta, float (&v)[4]) {
+  uint32_t r[4];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(ta));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
+}
+SD_DEV void tmem_st4(uint32_t ta, const float (&v)[4]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(ta), "r"(__float_as_uint(v[0])),
+               "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3]))
+               : "memory");
+}
+// N consecutive columns (N = 4, 8, 16 or 32) of this thread's lane
+template <int N>
+SD_DEV void tmem_ldn(uint32_t ta, float (&v)[N]) {
+  static_assert(N == 4 || N == 8 || N == 16 || N == 32, "4, 8, 16 or 32 columns");
+  if constexpr (N == 32) {
+    tmem_ld16(ta, reinterpret_cast<float(&)[16]>(v[0]));
+    tmem_ld16(ta + 16, reinterpret_cast<float(&)[16]>(v[16]));
+  } else if constexpr (N == 16) {
+    tmem_ld16(ta, v);
+  } else if constexpr (N == 8) {
+    tmem_ld8(ta, v);
+  } else {
+    tmem_ld4(ta, v);
+  }
+}
+template <int N>
+SD_DEV void tmem_stn(uint32_t ta, const float (&v)[N]) {
+  static_assert(N == 4 || N == 8 || N == 16 || N == 32, "4, 8, 16 or 32 columns");
+  if constexpr (N == 32) {
+    tmem_st16(ta, reinterpret_cast<const float(&)[16]>(v[0]));
+    tmem_st16(ta + 16, reinterpret_cast<const float(&)[16]>(v[16]));
+  } else if constexpr (N == 16) {
+    tmem_st16(ta, v);
+  } else if constexpr (N == 8) {
+    tmem_st8(ta, v);
+  } else {
+    tmem_st4(ta, v);
+  }
+}
 SD_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 SD_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 

@@ -60,14 +60,14 @@ def _paged_case(lens, q_lens, H, KV, D, fp8, seed):
 
 
 @pytest.mark.parametrize("fp8", [False, True])
-@pytest.mark.parametrize("S", [1, 5])
+@pytest.mark.parametrize("S", [1, 2, 5])
 @pytest.mark.parametrize("T", [5, 16, 17, 100, 2048, 8192])
 def test_paged_attention_single_sequence(fp8, S, T):
     got, ref, *_ = _paged_case([T], [S], 12, 2, 128, fp8, seed=T * 10 + S)
     assert_close_attention(got, ref, f"fp8={fp8} S={S} T={T}")
 
 
-@pytest.mark.parametrize("S", [1, 5])
+@pytest.mark.parametrize("S", [1, 2, 5])
 def test_paged_attention_draft_geometry(S):
     got, ref, *_ = _paged_case([333, 64], [S, S], 14, 2, 64, False, seed=3 + S)
     assert_close_attention(got, ref, f"14:2 d64 S={S}")
