@@ -43,6 +43,15 @@ struct WorkItem {             // 48 bytes
   int32_t cta;                // the persistent CTA that processes the item
 };
 static_assert(sizeof(WorkItem) == 48, "work item is 48 bytes");
+// What a persistent CTA's producer needs before its first copies: its first work
+// item and that item's first 32 page ids (0 past the item), one 256-byte load.
+struct CtaDesc {
+  WorkItem first;
+  int32_t pad0[4];
+  int32_t pages[32];
+  int32_t pad1[16];
+};
+static_assert(sizeof(CtaDesc) == 256, "CTA descriptor is 256 bytes");
 struct GroupInfo {
   int32_t first_item, nsplit, b, h, q0, nq, pad0, pad1;
 };
@@ -62,7 +71,7 @@ constexpr int kStatRows = 5;
 constexpr int kMergeWide = 16;  // groups with at least this many splits are merged by whole CTAs
 
 struct WsLayout {
-  size_t items, groups, ctas, mlist, lse, po, total;
+  size_t items, groups, ctas, cdesc, mlist, lse, po, total;
   int32_t max_items, max_groups;
 };
 
@@ -73,7 +82,8 @@ static WsLayout ws_layout(int B, int KV, int max_qtiles, int D, int target_items
   w.items = sizeof(PlanHeader);
   w.groups = align_up(w.items + sizeof(WorkItem) * (size_t)w.max_items, 256);
   w.ctas = align_up(w.groups + sizeof(GroupInfo) * (size_t)w.max_groups, 256);
-  w.mlist = align_up(w.ctas + sizeof(int32_t) * (size_t)(target_items / 4 + 1), 256);
+  w.cdesc = align_up(w.ctas + sizeof(int32_t) * (size_t)(target_items / 4 + 1), 256);
+  w.mlist = align_up(w.cdesc + sizeof(CtaDesc) * (size_t)(target_items / 4 + 1), 256);
   w.lse = align_up(w.mlist + sizeof(GroupInfo) * (size_t)w.max_groups, 256);
   w.po = align_up(w.lse + sizeof(float) * kStatRows * kMaxRows * (size_t)w.max_items, 256);
   w.total = align_up(w.po + sizeof(float) * kMaxRows * (size_t)D * w.max_items, 256);
@@ -99,6 +109,7 @@ struct AttnParams {
   WorkItem* items;
   GroupInfo* groups;
   int32_t* cta_first;  // [C + 1]: items of persistent CTA c are cta_first[c] .. cta_first[c+1]-1
+  CtaDesc* cdesc;      // [C]: first item and page ids of every CTA
   GroupInfo* merge_list;  // [max_groups]: the groups with more than one split (see PlanHeader)
   float* p_stat;  // [item][kStatRows][kMaxRows]: row max, then key-quarter sums
   float* p_o;
@@ -279,6 +290,18 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
       if (p.items[mid].cta < c) lo = mid + 1; else hi = mid;
     }
     p.cta_first[c] = lo;
+  }
+  __syncthreads();
+  // per-CTA descriptors: thread t fills page slot t % 32 of CTA t / 32
+  for (int u = threadIdx.x; u < grid * 32; u += blockDim.x) {
+    const int c = u >> 5, k = u & 31;
+    const int i0 = p.cta_first[c];
+    if (i0 >= p.cta_first[c + 1]) continue;  // no work
+    const WorkItem it = p.items[i0];
+    if (k == 0) p.cdesc[c].first = it;
+    p.cdesc[c].pages[k] = (p.page_table != nullptr && k < it.page_end - it.page_begin)
+                              ? p.page_table[static_cast<int64_t>(it.b) * p.max_pages + it.page_begin + k]
+                              : 0;
   }
   if (threadIdx.x == 0) {
     p.hdr->num_items = carry;
@@ -710,6 +733,7 @@ static int fill_workspace(AttnParams& p, void* ws, size_t ws_bytes, int B, int K
   p.items = reinterpret_cast<WorkItem*>(base + w.items);
   p.groups = reinterpret_cast<GroupInfo*>(base + w.groups);
   p.cta_first = reinterpret_cast<int32_t*>(base + w.ctas);
+  p.cdesc = reinterpret_cast<CtaDesc*>(base + w.cdesc);
   p.merge_list = reinterpret_cast<GroupInfo*>(base + w.mlist);
   p.p_stat = reinterpret_cast<float*>(base + w.lse);
   p.p_o = reinterpret_cast<float*>(base + w.po);
