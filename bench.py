@@ -45,16 +45,16 @@ H, KV, D = 12, 2, 128
 LAYERS = 28
 PAGE = 16
 # DRAM bytes (read + write) of one verify-kernel launch of the headline workload, from an
-# `ncu --set full` capture of `bench.py --profile-case verify8k` (8,490,496 read + 0 written)
-NCU_TRAFFIC_VERIFY8K = 8490496
+# `ncu --set full` capture of `bench.py --profile-case verify8k` (8,545,792 read + 0 written)
+NCU_TRAFFIC_VERIFY8K = 8545792
 
 
-def attn_bytes(T: int, q: int, fp8: bool, heads: int = H) -> float:
+def attn_bytes(T: int, q: int, fp8: bool, heads: int = H, d: int = D) -> float:
     pt = math.ceil(T / PAGE) * 4
-    qo = 2 * heads * q * D * 2
+    qo = 2 * heads * q * d * 2
     if fp8:
-        return T * KV * D * 2 + T * KV * D + T * KV * 4 + pt + qo
-    return T * KV * D * 4 + pt + qo
+        return T * KV * d * 2 + T * KV * d + T * KV * 4 + pt + qo
+    return T * KV * d * 4 + pt + qo
 
 
 # ------------------------------------------------------------------------------ clocks
@@ -160,7 +160,7 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
-def filled_cache(num_layers, lens, fp8, seed):
+def filled_cache(num_layers, lens, fp8, seed, d=D):
     """A paged cache of `num_layers` layers whose sequences hold `lens` seeded tokens
     (K ~ N(0,1); V ~ N(0,1), with 1 % +-8 sigma outliers for the E4M3 config)."""
     import torch
@@ -169,7 +169,7 @@ def filled_cache(num_layers, lens, fp8, seed):
     from specdec_b200.kernels import ops
 
     cap = max(lens)
-    cache = PagedKVCache.allocate(num_layers, len(lens), KV, D, cap, v_dtype="e4m3" if fp8 else "bf16",
+    cache = PagedKVCache.allocate(num_layers, len(lens), KV, d, cap, v_dtype="e4m3" if fp8 else "bf16",
                                   device="cuda", page_order_seed=seed)
     g = torch.Generator(device="cuda").manual_seed(seed)
     total = sum(lens)
@@ -177,8 +177,8 @@ def filled_cache(num_layers, lens, fp8, seed):
     n_new = torch.tensor(lens, dtype=torch.int32, device="cuda")
     pos0 = torch.zeros(len(lens), dtype=torch.int32, device="cuda")
     for layer in range(num_layers):
-        k = torch.randn(total, KV, D, generator=g, device="cuda").to(torch.bfloat16)
-        v = torch.randn(total, KV, D, generator=g, device="cuda")
+        k = torch.randn(total, KV, d, generator=g, device="cuda").to(torch.bfloat16)
+        v = torch.randn(total, KV, d, generator=g, device="cuda")
         if fp8:
             hit = torch.rand(v.shape, generator=g, device="cuda") < 0.01
             sgn = torch.where(torch.rand(v.shape, generator=g, device="cuda") < 0.5, -8.0, 8.0)
@@ -193,7 +193,7 @@ def filled_cache(num_layers, lens, fp8, seed):
 class GraphStep:
     """One verify/decode pass over every layer: device plan + per-layer paged attention, in a CUDA graph."""
 
-    def __init__(self, cache, q_lens, ctx_lens, seed=0, events=False):
+    def __init__(self, cache, q_lens, ctx_lens, seed=0, events=False, heads=H):
         import torch
 
         from specdec_b200.kernels import ops
@@ -202,10 +202,10 @@ class GraphStep:
         self.batch = ops.RaggedBatch.from_lengths(q_lens, ctx_lens)
         L = cache.num_layers
         g = torch.Generator(device="cuda").manual_seed(seed + 1)
-        self.q = [torch.randn(self.batch.total_rows, H, D, generator=g, device="cuda").to(torch.bfloat16)
+        self.q = [torch.randn(self.batch.total_rows, heads, cache.head_dim, generator=g, device="cuda").to(torch.bfloat16)
                   for _ in range(L)]
         self.out = [torch.empty_like(x) for x in self.q]
-        self.ws = ops.attn_workspace(self.batch, H, cache)
+        self.ws = ops.attn_workspace(self.batch, heads, cache)
         self.status = torch.zeros(1, dtype=torch.int32, device="cuda")
         self.events = ([(torch.cuda.Event(enable_timing=True, external=True),
                          torch.cuda.Event(enable_timing=True, external=True)) for _ in range(L)]
@@ -290,6 +290,24 @@ def measure_ragged(steps, warmup, seed=4):
     step = GraphStep(cache, q_lens, lens, seed)
     ms = time_steps(step, steps, warmup, 1)
     byt = 2 * sum(attn_bytes(t, q, True) for t, q in zip(lens, q_lens))
+    st = int(step.status.item())
+    del step, cache
+    torch.cuda.empty_cache()
+    if st:
+        raise RuntimeError(f"device status {st:#x}")
+    return byt * steps / (ms * 1e-3) / 1e9, ms / steps, byt / 2
+
+
+def measure_draft(steps, warmup, seed=5):
+    """Draft-model decode attention (Qwen2.5-0.5B geometry: 14:2 heads, head_dim 64, bf16 K/V):
+    64 sequences at context 8192, q_len 1, one launch per layer over 2 layer caches."""
+    import torch
+
+    lens, q_lens = [8192] * 64, [1] * 64
+    cache = filled_cache(2, lens, False, seed, d=64)
+    step = GraphStep(cache, q_lens, lens, seed, heads=14)
+    ms = time_steps(step, steps, warmup, 1)
+    byt = 2 * sum(attn_bytes(t, q, False, heads=14, d=64) for t, q in zip(lens, q_lens))
     st = int(step.status.item())
     del step, cache
     torch.cuda.empty_cache()
@@ -484,6 +502,9 @@ def run_ours(args, world, rank, local):
         gbs, mss, byt = measure_ragged(max(20, min(args.steps, 200)), 5)
         extras["ragged64_e4m3v"] = {"GB/s": round(gbs, 1), "pct_of_8TBs": round(gbs / 80.0, 2),
                                     "ms_per_layer": round(mss / 2, 4), "bytes_per_layer": int(byt)}
+        gbs, mss, byt = measure_draft(max(20, min(args.steps, 200)), 5)
+        extras["draft64_d64_q1_T8192"] = {"GB/s": round(gbs, 1), "pct_of_8TBs": round(gbs / 80.0, 2),
+                                          "ms_per_layer": round(mss / 2, 4), "bytes_per_layer": int(byt)}
     if not args.no_extras:
         e_gbs, e_ms, h2d, d2h = measure_e2e(max(5, min(args.steps, 100)), 3)
         e2e = {"value": round(e_gbs * world, 3), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
@@ -539,6 +560,9 @@ def run_profile_case(args):
     if args.profile_case == "verify8k":
         cache = filled_cache(LAYERS, [8192], False, 0)
         step = GraphStep(cache, [5], [8192], 0)
+    elif args.profile_case == "draft64":
+        cache = filled_cache(2, [8192] * 64, False, 5, d=64)
+        step = GraphStep(cache, [1] * 64, [8192] * 64, 5, heads=14)
     else:
         g = torch.Generator().manual_seed(4)
         lens = [int(x) for x in torch.randint(1024, 8193, (64,), generator=g)]
@@ -568,7 +592,7 @@ def main():
     ap.add_argument("--specdec-seqs", type=int, default=256)
     ap.add_argument("--specdec-prompt", type=int, default=8192)
     ap.add_argument("--specdec-new", type=int, default=64)
-    ap.add_argument("--profile-case", choices=["verify8k", "ragged64", "ragged64-bf16"], default=None,
+    ap.add_argument("--profile-case", choices=["verify8k", "ragged64", "ragged64-bf16", "draft64"], default=None,
                     help="only replay this workload's step graph warmup + steps times (for profilers)")
     args = ap.parse_args()
     if args.profile_case:
