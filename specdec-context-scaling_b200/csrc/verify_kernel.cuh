@@ -57,7 +57,7 @@ struct V3Geom {
   static constexpr int VC_OFF = ((S_OFF + NS * ST + 1023) / 1024) * 1024;  // widened V (E4M3 only)
   static constexpr int Q_OFF = VC_OFF + (VF8 ? 2 * 32768 : 0);
   static constexpr int QH = NR * 128;                    // one dim half of Q: [NR rows][128 B]
-  static constexpr int QB = NR * 256;                    // one P buffer: [2 key halves][NR rows][128 B]
+  static constexpr int QB = NR * 256;                    // one P buffer: [128 keys][NR rows x 2 B], MN-major
   static constexpr int P_OFF = Q_OFF + KH * QH;
   static constexpr int SMEM = P_OFF + 2 * QB + 1024;     // + alignment slack
   static constexpr int TMEM_COLS = NR <= 16 ? 64 : 128;  // S[2] + O = 3 NR columns

@@ -116,12 +116,15 @@ def test_plan_reuse_across_layers():
     assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("fp8,D", [(False, 128), (True, 128), (False, 64)])
-def test_history_ready_gives_identical_results(fp8, D):
+@pytest.mark.parametrize("fp8,D,q_lens", [(False, 128, [5, 1, 2, 5]), (True, 128, [5, 1, 2, 5]),
+                                          (False, 64, [5, 1, 2, 5]), (True, 128, [1, 1, 1, 1]),
+                                          (False, 64, [1, 2, 1, 1])])
+def test_history_ready_gives_identical_results(fp8, D, q_lens):
     """Loading the plan, page table and KV history before the dependency wait changes
-    no result: a layer stack with history_ready equals the same calls without it."""
+    no result: a layer stack with history_ready equals the same calls without it (verify
+    rows, decode rows, and the draft's q = 2 catch-up)."""
     ops = _ops()
-    lens, q_lens = [900, 4100, 33, 2000], [5, 1, 2, 5]
+    lens = [900, 4100, 33, 2000]
     H = 12 if D == 128 else 14
     cache, ks, vrefs = build_cache(lens, 2, D, fp8=fp8, seed=9, num_layers=3)
     batch = ops.RaggedBatch.from_lengths(q_lens, lens)
