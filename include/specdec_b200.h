@@ -288,8 +288,9 @@ int specdec_apply_rope(const void* x, int64_t stride_b, int64_t stride_h, int64_
 /* out = silu(gate) * up, elementwise. */
 int specdec_swiglu(const void* gate, const void* up, void* out, int32_t dtype, int64_t n,
                    specdec_stream_t stream);
-/* SwiGLU of a fused gate|up projection (rows, 2 inter) bf16 -> (rows, inter), the
- * rounding of specdec_swiglu; inter % 8 == 0, 16-byte aligned rows. */
+/* SwiGLU of a fused gate|up projection (rows, 2 inter) bf16 -> (rows, inter):
+ * bf16(bf16(silu(g)) * u) with silu from the hardware exponential and reciprocal (at most
+ * one bf16 ulp from specdec_swiglu); inter % 8 == 0, 16-byte aligned rows. */
 int specdec_swiglu_packed(const void* gate_up, void* out, int64_t rows, int64_t inter, specdec_stream_t stream);
 
 /* Diagnostics. */
