@@ -152,6 +152,8 @@ SD_DEV void rope_lane(const __nv_bfloat16* src, const __nv_bfloat16* cs, const _
 template <int D, bool VF8>
 __global__ void __launch_bounds__(256) rope_append_kernel(const RopeAppendParams rp) {
   constexpr int PER = D / 32;
+  grid_dep_wait();  // launched programmatically: qkv is the preceding work's output
+  grid_dep_launch();
   const AppendParams& p = rp.a;
   const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -332,13 +334,7 @@ extern "C" int specdec_rope_append(const SpecdecRopeAppendArgs* a, specdec_strea
   const int64_t blocks = (warps * 32 + 255) / 256;
   if (blocks > 0x7fffffff) return fail(SPECDEC_ERR_INVALID, "batch too large");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (D == 128) {
-    if (vf8)
-      rope_append_kernel<128, true><<<static_cast<unsigned>(blocks), 256, 0, st>>>(rp);
-    else
-      rope_append_kernel<128, false><<<static_cast<unsigned>(blocks), 256, 0, st>>>(rp);
-  } else {
-    rope_append_kernel<64, false><<<static_cast<unsigned>(blocks), 256, 0, st>>>(rp);
-  }
-  return after_launch("rope_append_kernel");
+  auto* kern = D == 128 ? (vf8 ? rope_append_kernel<128, true> : rope_append_kernel<128, false>)
+                        : rope_append_kernel<64, false>;
+  return launch_pdl("rope_append_kernel", kern, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st, rp);
 }

@@ -74,6 +74,8 @@ __global__ void __launch_bounds__(256) rmsnorm_warp_kernel(const __nv_bfloat16* 
                                                            const __nv_bfloat16* __restrict__ w,
                                                            __nv_bfloat16* __restrict__ y, int64_t rows, int hidden,
                                                            float eps) {
+  grid_dep_wait();  // launched programmatically: x is the preceding work's output
+  grid_dep_launch();
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -155,6 +157,8 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const T* __restrict__ g, co
 __global__ void __launch_bounds__(256) swiglu_packed_kernel(const __nv_bfloat16* __restrict__ gu,
                                                             __nv_bfloat16* __restrict__ y, int64_t rows,
                                                             int64_t inter) {
+  grid_dep_wait();  // launched programmatically: gu is the preceding work's output
+  grid_dep_launch();
   const int64_t n8 = rows * (inter / 8);
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -191,9 +195,9 @@ extern "C" int specdec_swiglu_packed(const void* gate_up, void* out, int64_t row
   if (n8 == 0) return SPECDEC_OK;
   int64_t blocks = (n8 + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
-  swiglu_packed_kernel<<<static_cast<unsigned>(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(gate_up), static_cast<__nv_bfloat16*>(out), rows, inter);
-  return after_launch("swiglu_packed_kernel");
+  return launch_pdl("swiglu_packed_kernel", swiglu_packed_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+                    reinterpret_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(gate_up),
+                    static_cast<__nv_bfloat16*>(out), rows, inter);
 }
 
 extern "C" int specdec_rmsnorm(const void* x, const void* weight, void* out, int32_t dtype, int64_t rows,
@@ -212,17 +216,12 @@ extern "C" int specdec_rmsnorm(const void* x, const void* weight, void* out, int
     const auto* xb = static_cast<const __nv_bfloat16*>(x);
     const auto* wb = static_cast<const __nv_bfloat16*>(weight);
     auto* yb = static_cast<__nv_bfloat16*>(out);
-    if (ch <= 1)
-      rmsnorm_warp_kernel<1><<<blocks, 256, 0, st>>>(xb, wb, yb, rows, hidden, eps);
-    else if (ch <= 2)
-      rmsnorm_warp_kernel<2><<<blocks, 256, 0, st>>>(xb, wb, yb, rows, hidden, eps);
-    else if (ch <= 4)
-      rmsnorm_warp_kernel<4><<<blocks, 256, 0, st>>>(xb, wb, yb, rows, hidden, eps);
-    else if (ch <= 8)
-      rmsnorm_warp_kernel<8><<<blocks, 256, 0, st>>>(xb, wb, yb, rows, hidden, eps);
-    else
-      rmsnorm_warp_kernel<16><<<blocks, 256, 0, st>>>(xb, wb, yb, rows, hidden, eps);
-    return after_launch("rmsnorm_warp_kernel");
+    auto* kern = ch <= 1 ? rmsnorm_warp_kernel<1>
+                 : ch <= 2 ? rmsnorm_warp_kernel<2>
+                 : ch <= 4 ? rmsnorm_warp_kernel<4>
+                 : ch <= 8 ? rmsnorm_warp_kernel<8>
+                           : rmsnorm_warp_kernel<16>;
+    return launch_pdl("rmsnorm_warp_kernel", kern, dim3(blocks), dim3(256), 0, st, xb, wb, yb, rows, hidden, eps);
   }
   if (dtype == SPECDEC_F32)
     rmsnorm_kernel<float><<<static_cast<unsigned>(rows), 256, 0, st>>>(
