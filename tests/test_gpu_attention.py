@@ -101,6 +101,34 @@ def test_ragged_decode_rows(fp8, H, D):
     assert_close_attention(got, ref, f"decode rows fp8={fp8} H={H} D={D}")
 
 
+def test_ragged_config4_full_size():
+    """The ragged config at its full size (64 sequences, T ~ U[1024, 8192], q_len 1 and 5
+    in a 1:1 seeded shuffle, E4M3 V): every output row against the oracle."""
+    g = torch.Generator().manual_seed(4)
+    lens = [int(x) for x in torch.randint(1024, 8193, (64,), generator=g)]
+    q_lens = [1, 5] * 32
+    perm = torch.randperm(64, generator=g).tolist()
+    q_lens = [q_lens[i] for i in perm]
+    ops = _ops()
+    cache, ks, vrefs = build_cache(lens, 2, 128, fp8=True, seed=4, over_provision=1)
+    batch = ops.RaggedBatch.from_lengths(q_lens, lens)
+    q = torch.randn(batch.total_rows, 12, 128, generator=torch.Generator().manual_seed(11)).to(torch.bfloat16)
+    got = ops.paged_attention(q.cuda(), cache, 0, batch).cpu()
+    assert_close_attention(got, oracle_rows(q, ks, vrefs, q_lens), "ragged config 4")
+
+
+def test_draft_decode_full_size():
+    """The draft model's decode attention at the bench's size (64 sequences x 8192, q_len 1,
+    14:2 heads, head_dim 64, bf16 K/V): every output row against the oracle."""
+    ops = _ops()
+    lens, q_lens = [8192] * 64, [1] * 64
+    cache, ks, vrefs = build_cache(lens, 2, 64, fp8=False, seed=5, over_provision=1)
+    batch = ops.RaggedBatch.from_lengths(q_lens, lens)
+    q = torch.randn(batch.total_rows, 14, 64, generator=torch.Generator().manual_seed(12)).to(torch.bfloat16)
+    got = ops.paged_attention(q.cuda(), cache, 0, batch).cpu()
+    assert_close_attention(got, oracle_rows(q, ks, vrefs, q_lens), "draft decode 64 x 8K")
+
+
 def test_plan_reuse_across_layers():
     """One plan serves every layer: reuse_plan=True gives the same output as a fresh plan."""
     ops = _ops()
