@@ -32,6 +32,10 @@ constexpr int kCvtWarps = 4;
 // threads of one CTA: softmax, producer, MMA (+ converters for E4M3 V)
 template <bool VF8>
 constexpr int v3_threads() { return 32 * (kSmWarps + 2 + (VF8 ? kCvtWarps : 0)); }
+// register budget per thread: each SM sub-partition holds 16384 registers and ceil(warps / 4)
+// of the CTA's warps (allocation in steps of 8 per thread)
+template <bool VF8>
+constexpr int v3_max_regs() { return (16384 / (32 * ((v3_threads<VF8>() / 32 + 3) / 4))) & ~7; }
 constexpr int kTileKeys = 128;
 constexpr int kTilePages = 8;
 constexpr float kRescaleLog2 = 8.f;   // lazy rescale threshold (log2 units)
