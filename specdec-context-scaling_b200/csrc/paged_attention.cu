@@ -183,8 +183,13 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
   __shared__ long long s_total;
   __shared__ int s_first[1024], s_pages[1024], s_nq[1024], s_c0[1024];
   __shared__ long long s_start[1024];
+  // each persistent CTA's first item (index and copy), recorded as the items are written
+  constexpr int kPlanCtas = 192;
+  __shared__ int s_cfirst[kPlanCtas + 1];
+  __shared__ WorkItem s_fitem[kPlanCtas];
   const int ngroups = p.max_groups;
   if (threadIdx.x == 0) s_total = 0;
+  for (int c = threadIdx.x; c <= kPlanCtas; c += blockDim.x) s_cfirst[c] = -1;  // -1: no item
   __syncthreads();
   long long local = 0;
   for (int gi = threadIdx.x; gi < ngroups; gi += blockDim.x) {
@@ -275,6 +280,11 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
       it.row0 = seq_row0(p, b2);
       it.cta = c;
       p.items[carry + i] = it;
+      // range c starts inside this group: this is CTA c's first item
+      if (range_lo(c) >= gs && c < kPlanCtas) {
+        s_cfirst[c] = carry + i;
+        s_fitem[c] = it;
+      }
     }
     __syncthreads();
     carry += chunk_total;
@@ -282,22 +292,30 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
     ncarry += chunk_narrow;
     pcarry += chunk_pages;
   }
-  // first item of every CTA of the grid (items are ordered by CTA): cta_first[c] .. cta_first[c+1]
+  // first item of every CTA of the grid (items are ordered by CTA): cta_first[c] .. cta_first[c+1];
+  // the CTAs past C have none
+  const bool recorded = grid <= kPlanCtas;
   for (int c = threadIdx.x; c <= grid; c += blockDim.x) {
-    int lo = 0, hi = carry;
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (p.items[mid].cta < c) lo = mid + 1; else hi = mid;
+    int first;
+    if (recorded) {
+      first = (c < C && s_cfirst[c] >= 0) ? s_cfirst[c] : carry;
+    } else {
+      int lo = 0, hi = carry;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (p.items[mid].cta < c) lo = mid + 1; else hi = mid;
+      }
+      first = lo;
     }
-    p.cta_first[c] = lo;
+    p.cta_first[c] = first;
   }
   __syncthreads();
   // per-CTA descriptors: thread t fills page slot t % 32 of CTA t / 32
-  for (int u = threadIdx.x; u < grid * 32; u += blockDim.x) {
+  for (int u = threadIdx.x; u < C * 32; u += blockDim.x) {
     const int c = u >> 5, k = u & 31;
-    const int i0 = p.cta_first[c];
-    if (i0 >= p.cta_first[c + 1]) continue;  // no work
-    const WorkItem it = p.items[i0];
+    // no work (no pages at all, P == 0): the CTA reads no descriptor
+    if (recorded ? s_cfirst[c] < 0 : p.cta_first[c] >= p.cta_first[c + 1]) continue;
+    const WorkItem it = recorded ? s_fitem[c] : p.items[p.cta_first[c]];
     if (k == 0) p.cdesc[c].first = it;
     p.cdesc[c].pages[k] = (p.page_table != nullptr && k < it.page_end - it.page_begin)
                               ? p.page_table[static_cast<int64_t>(it.b) * p.max_pages + it.page_begin + k]
