@@ -43,11 +43,12 @@ struct WorkItem {             // 48 bytes
   int32_t cta;                // the persistent CTA that processes the item
 };
 static_assert(sizeof(WorkItem) == 48, "work item is 48 bytes");
-// What a persistent CTA's producer needs before its first copies: its first work
-// item and that item's first 32 page ids (0 past the item), one 256-byte load.
+// What a persistent CTA needs before its first copies: its item range, its first work
+// item and that item's first 32 page ids (0 past the item), one 256-byte line.
 struct CtaDesc {
   WorkItem first;
-  int32_t pad0[4];
+  int32_t item_begin, item_end;  // the CTA's items: [item_begin, item_end) (every CTA of the grid)
+  int32_t pad0[2];
   int32_t pages[32];
   int32_t pad1[16];
 };
@@ -59,15 +60,17 @@ struct PlanHeader {
   int32_t num_items, pages_per_split, num_groups, total_pages;
   int32_t num_merge_wide;    // split groups with >= kMergeWide splits: merge_list[0 ..)
   int32_t num_merge_narrow;  // other split groups: merge_list[max_groups - 1], [max_groups - 2], ...
-  int32_t pad0[26];
+  int32_t num_ctas;          // CTAs of the verify grid that get pages: 0 .. num_ctas - 1
+  int32_t pad0[25];
   unsigned long long bar_arrive;  // grid-barrier arrivals of the verify kernel (own 128-byte line)
   int32_t pad1[30];
 };
 static_assert(sizeof(PlanHeader) == 256, "plan header is 256 bytes");
 
 constexpr int kMaxRows = 64;  // query rows (n_rep x query positions) per work item
-// per split item and row: the row max (log2 units) and four key-quarter partial sums
-constexpr int kStatRows = 5;
+// per split item and row, one 32-byte sector: the row max (log2 units), the four
+// key-quarter partial sums and three unused words
+constexpr int kStatStride = 8;
 constexpr int kMergeWide = 16;  // groups with at least this many splits are merged by whole CTAs
 
 struct WsLayout {
@@ -85,7 +88,7 @@ static WsLayout ws_layout(int B, int KV, int max_qtiles, int D, int target_items
   w.cdesc = align_up(w.ctas + sizeof(int32_t) * (size_t)(target_items / 4 + 1), 256);
   w.mlist = align_up(w.cdesc + sizeof(CtaDesc) * (size_t)(target_items / 4 + 1), 256);
   w.lse = align_up(w.mlist + sizeof(GroupInfo) * (size_t)w.max_groups, 256);
-  w.po = align_up(w.lse + sizeof(float) * kStatRows * kMaxRows * (size_t)w.max_items, 256);
+  w.po = align_up(w.lse + sizeof(float) * kStatStride * kMaxRows * (size_t)w.max_items, 256);
   w.total = align_up(w.po + sizeof(float) * kMaxRows * (size_t)D * w.max_items, 256);
   return w;
 }
@@ -111,7 +114,7 @@ struct AttnParams {
   int32_t* cta_first;  // [C + 1]: items of persistent CTA c are cta_first[c] .. cta_first[c+1]-1
   CtaDesc* cdesc;      // [C]: first item and page ids of every CTA
   GroupInfo* merge_list;  // [max_groups]: the groups with more than one split (see PlanHeader)
-  float* p_stat;  // [item][kStatRows][kMaxRows]: row max, then key-quarter sums
+  float* p_stat;  // [item][kMaxRows][kStatStride]: row max, then key-quarter sums
   float* p_o;
   int32_t max_items, max_groups, target_items;
   int32_t tile_pages;  // the verify kernel consumes keys in tiles of this many pages
@@ -310,6 +313,10 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
     p.cta_first[c] = first;
   }
   __syncthreads();
+  for (int c = threadIdx.x; c < grid; c += blockDim.x) {
+    p.cdesc[c].item_begin = p.cta_first[c];
+    p.cdesc[c].item_end = p.cta_first[c + 1];
+  }
   // per-CTA descriptors: thread t fills page slot t % 32 of CTA t / 32
   for (int u = threadIdx.x; u < C * 32; u += blockDim.x) {
     const int c = u >> 5, k = u & 31;
@@ -329,6 +336,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
     p.hdr->num_merge_wide = wcarry;
     p.hdr->num_merge_narrow = ncarry;
     p.hdr->total_pages = static_cast<int32_t>(P);
+    p.hdr->num_ctas = C;
   }
 }
 
@@ -367,7 +375,7 @@ SD_DEV void merge_combine(MergeState& st, const MergeState& o) {
 // before the grid barrier.
 template <int D, int NWARP>
 SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int warp, int lane, int n_wide, int n_narrow,
-                         const GroupInfo& pre_w, const GroupInfo& pre_n) {
+                         int n_ctas, const GroupInfo& pre_w, const GroupInfo& pre_n) {
   constexpr int NQ = D / 4;     // dim quads
   constexpr int SPW = 32 / NQ;  // split slots per warp
   const int quad = lane % NQ, slot = lane / NQ;
@@ -388,11 +396,11 @@ SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int warp, int la
         const int sk = s + k * step;
         const bool in = sk < grp.nsplit;
         const int64_t item = static_cast<int64_t>(grp.first_item) + sk;
-        const float* st_row = p.p_stat + item * (kStatRows * kMaxRows) + r;
-        ms[k] = in ? __ldcg(st_row) : -INFINITY;
-        ls[k] = in ? (__ldcg(st_row + kMaxRows) + __ldcg(st_row + 2 * kMaxRows)) +
-                         (__ldcg(st_row + 3 * kMaxRows) + __ldcg(st_row + 4 * kMaxRows))
-                   : 0.f;
+        const float* st_row = p.p_stat + (item * kMaxRows + r) * kStatStride;  // one sector
+        const float4 st4 = in ? __ldcg(reinterpret_cast<const float4*>(st_row)) : make_float4(-INFINITY, 0.f, 0.f, 0.f);
+        const float l3 = in ? __ldcg(st_row + 4) : 0.f;
+        ms[k] = st4.x;
+        ls[k] = (st4.y + st4.z) + (st4.w + l3);
         v[k] = in ? __ldcg(reinterpret_cast<const float4*>(p.p_o + (item * kMaxRows + r) * D) + quad)
                   : make_float4(0.f, 0.f, 0.f, 0.f);
       }
@@ -441,7 +449,7 @@ SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int warp, int la
   };
 
   // wide rows: one CTA each
-  for (int u = blockIdx.x; u < wide_units; u += gridDim.x) {
+  for (int u = blockIdx.x; u < wide_units; u += n_ctas) {
     const GroupInfo grp = u == static_cast<int>(blockIdx.x) ? pre_w : p.merge_list[u / RU];
     const int r = u % RU;
     if (r >= p.n_rep * grp.nq) continue;  // uniform per CTA
@@ -477,7 +485,7 @@ SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int warp, int la
   }
   // narrow rows: one warp each
   const int u0 = blockIdx.x * NWARP + warp;
-  for (int u = u0; u < narrow_units; u += gridDim.x * NWARP) {
+  for (int u = u0; u < narrow_units; u += n_ctas * NWARP) {
     const GroupInfo grp = u == u0 ? pre_n : p.merge_list[p.max_groups - 1 - u / RU];
     const int r = u % RU;
     if (r >= p.n_rep * grp.nq) continue;  // uniform per warp
@@ -1027,9 +1035,10 @@ __global__ void __launch_bounds__(128) gather4_selftest_kernel(const __grid_cons
   }
   __syncthreads();
   if (threadIdx.x == 0) {
+    const uint64_t pol = l2_evict_first();
     mbar_arrive_expect_tx(&bar, 8192 + 256);
-    tma_gather4(buf, &big, 0, rows.x, rows.y, rows.z, rows.w, &bar);
-    tma_gather4(buf + 8192, &small, 0, rows.x, rows.y, rows.z, rows.w, &bar);
+    tma_gather4(buf, &big, 0, rows.x, rows.y, rows.z, rows.w, &bar, pol);
+    tma_gather4(buf + 8192, &small, 0, rows.x, rows.y, rows.z, rows.w, &bar, pol);
   }
   const bool ok = __all_sync(0xffffffffu, mbar_wait(&bar, 0));
   if (!ok) {

@@ -105,25 +105,33 @@ SD_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) 
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
-// 3-D tiled tensor load; c0 is the innermost (element) coordinate and must be a
-// multiple of 16 bytes / element size (callers pass 0 or 64 bf16 elements).
+// L2 policy for data read once per call (the KV stream): its lines are the first to go,
+// so the small tensors around it (queries, page tables, plans, split partials) stay in L2.
+SD_DEV uint64_t l2_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+// 3-D tiled tensor load with an L2 policy; c0 is the innermost (element) coordinate and
+// must be a multiple of 16 bytes / element size (callers pass 0 or 64 bf16 elements).
 SD_DEV void tma_load_3d(void* dst, const CUtensorMap* map, int32_t c0, int32_t c1, int32_t c2,
-                        uint64_t* bar) {
+                        uint64_t* bar, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
 // Four rows of a 2-D tensor map in one request (tile::gather4): rows r0 .. r3 starting
 // at element x (the map's box is one row high), written to dst as four consecutive
-// rows; completion is counted on the mbarrier.
+// rows; completion is counted on the mbarrier; `policy` is the L2 policy of the reads.
 SD_DEV void tma_gather4(void* dst, const CUtensorMap* map, int32_t x, int32_t r0, int32_t r1, int32_t r2, int32_t r3,
-                        uint64_t* bar) {
+                        uint64_t* bar, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar)),
+      "l"(policy)
       : "memory");
 }
 SD_DEV void prefetch_tmap(const CUtensorMap* map) {
