@@ -60,7 +60,7 @@ struct PlanHeader {
   int32_t num_items, pages_per_split, num_groups, total_pages;
   int32_t num_merge_wide;    // split groups with >= kMergeWide splits: merge_list[0 ..)
   int32_t num_merge_narrow;  // other split groups: merge_list[max_groups - 1], [max_groups - 2], ...
-  int32_t num_ctas;          // CTAs of the verify grid that get pages: 0 .. num_ctas - 1
+  int32_t num_ctas;          // CTAs that get pages: the last num_ctas blocks of the verify grid
   int32_t pad0[25];
   unsigned long long bar_arrive;  // grid-barrier arrivals of the verify kernel (own 128-byte line)
   int32_t pad1[30];
@@ -68,6 +68,8 @@ struct PlanHeader {
 static_assert(sizeof(PlanHeader) == 256, "plan header is 256 bytes");
 
 constexpr int kMaxRows = 64;  // query rows (n_rep x query positions) per work item
+constexpr int kPlanTilePages = 8;  // pages per 128-key tile of the verify kernel
+constexpr int kWholeTileMax = 4;   // the plan gives CTAs whole tiles up to this many per CTA
 // per split item and row, one 32-byte sector: the row max (log2 units), the four
 // key-quarter partial sums and three unused words
 constexpr int kStatStride = 8;
@@ -184,6 +186,7 @@ SD_DEV int block_exclusive_scan(int v, int& total, int* s_warp) {
 __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
   __shared__ int s_warp[32];
   __shared__ long long s_total;
+  __shared__ int s_rows;
   __shared__ int s_first[1024], s_pages[1024], s_nq[1024], s_c0[1024];
   __shared__ long long s_start[1024];
   // each persistent CTA's first item (index and copy), recorded as the items are written
@@ -191,28 +194,55 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
   __shared__ int s_cfirst[kPlanCtas + 1];
   __shared__ WorkItem s_fitem[kPlanCtas];
   const int ngroups = p.max_groups;
-  if (threadIdx.x == 0) s_total = 0;
+  if (threadIdx.x == 0) {
+    s_total = 0;
+    s_rows = 0;
+  }
   for (int c = threadIdx.x; c <= kPlanCtas; c += blockDim.x) s_cfirst[c] = -1;  // -1: no item
   __syncthreads();
   long long local = 0;
+  int lrows = 0;  // query rows of the groups with pages
   for (int gi = threadIdx.x; gi < ngroups; gi += blockDim.x) {
     int b, h, q0, nq;
-    local += group_pages(p, gi, b, h, q0, nq);
+    const int pg = group_pages(p, gi, b, h, q0, nq);
+    local += pg;
+    if (pg > 0) lrows += p.n_rep * nq;
   }
   // warp reduce then one atomic per warp
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
-  if ((threadIdx.x & 31) == 0) atomicAdd(reinterpret_cast<unsigned long long*>(&s_total),
-                                         static_cast<unsigned long long>(local));
+  for (int o = 16; o > 0; o >>= 1) {
+    local += __shfl_xor_sync(0xffffffffu, local, o);
+    lrows += __shfl_xor_sync(0xffffffffu, lrows, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicAdd(reinterpret_cast<unsigned long long*>(&s_total), static_cast<unsigned long long>(local));
+    atomicAdd(&s_rows, lrows);
+  }
   __syncthreads();
   const long long P = s_total;
   // Balanced split: the concatenation of every group's pages (groups in order) is
   // cut into C equal ranges, range c = [c*P/C, (c+1)*P/C) for CTA c of the
   // persistent kernel.  An item is the intersection of a range with a group, so
   // a group yields one item per range it meets: num_items <= C + groups.
-  // C <= P keeps every range non-empty (so no item is empty); the CTAs past C get no items
+  // C <= P keeps every range non-empty (so no item is empty); the CTAs past C get no items.
+  // Small calls (at most kWholeTileMax tiles per CTA, e.g. one sequence of a few thousand
+  // tokens) are latency-bound: there C is the fewest CTAs that each take k whole 128-key
+  // tiles (an 8192-token sequence: 2 x 64 CTAs of one tile, not 148 of 7 pages), so no CTA
+  // pays a tile's latency for a fraction of one and the merge has fewer splits -- but no
+  // fewer CTAs than split rows when the grid has that many, so the merge of rows split
+  // across many CTAs (a CTA each) still runs in one round.
   const int grid = p.target_items / 4;
-  const int C = static_cast<int>(min(static_cast<long long>(grid), max(P, 1LL)));
+  int C = static_cast<int>(min(static_cast<long long>(grid), max(P, 1LL)));
+  {
+    const long long tile_slots = static_cast<long long>(kPlanTilePages) * grid;
+    const long long k = (P + tile_slots - 1) / tile_slots;  // tiles per CTA with the whole grid
+    if (k >= 1 && k <= kWholeTileMax) {
+      const long long per = k * kPlanTilePages;
+      long long want = (P + per - 1) / per;
+      if (s_rows <= grid) want = max(want, static_cast<long long>(s_rows));
+      C = static_cast<int>(min(static_cast<long long>(C), want));
+    }
+  }
   auto cta_of = [&](long long pos) { return static_cast<int>(((pos + 1) * C + P - 1) / P) - 1; };
   auto range_lo = [&](int c) { return static_cast<long long>(c) * P / C; };
 
@@ -313,20 +343,26 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
     p.cta_first[c] = first;
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < grid; c += blockDim.x) {
-    p.cdesc[c].item_begin = p.cta_first[c];
-    p.cdesc[c].item_end = p.cta_first[c + 1];
+  // Descriptors by block: blocks 0 .. idle - 1 of the verify grid get no pages -- they are
+  // dispatched first and leave at once, so they never wait for an SM that a previous
+  // launch still holds -- and block idle + c runs CTA c's range
+  const int idle = grid - C;
+  for (int bx = threadIdx.x; bx < grid; bx += blockDim.x) {
+    const int c = bx - idle;
+    p.cdesc[bx].item_begin = c < 0 ? 0 : p.cta_first[c];
+    p.cdesc[bx].item_end = c < 0 ? 0 : p.cta_first[c + 1];
   }
-  // per-CTA descriptors: thread t fills page slot t % 32 of CTA t / 32
+  // first item and page ids: thread t fills page slot t % 32 of CTA t / 32
   for (int u = threadIdx.x; u < C * 32; u += blockDim.x) {
     const int c = u >> 5, k = u & 31;
     // no work (no pages at all, P == 0): the CTA reads no descriptor
     if (recorded ? s_cfirst[c] < 0 : p.cta_first[c] >= p.cta_first[c + 1]) continue;
     const WorkItem it = recorded ? s_fitem[c] : p.items[p.cta_first[c]];
-    if (k == 0) p.cdesc[c].first = it;
-    p.cdesc[c].pages[k] = (p.page_table != nullptr && k < it.page_end - it.page_begin)
-                              ? p.page_table[static_cast<int64_t>(it.b) * p.max_pages + it.page_begin + k]
-                              : 0;
+    CtaDesc& d = p.cdesc[idle + c];
+    if (k == 0) d.first = it;
+    d.pages[k] = (p.page_table != nullptr && k < it.page_end - it.page_begin)
+                     ? p.page_table[static_cast<int64_t>(it.b) * p.max_pages + it.page_begin + k]
+                     : 0;
   }
   if (threadIdx.x == 0) {
     p.hdr->num_items = carry;
@@ -370,11 +406,12 @@ SD_DEV void merge_combine(MergeState& st, const MergeState& o) {
 }
 
 // s_st: NWARP x 32 states of shared memory (the caller's free staging area).
+// cta: the caller's place among the n_ctas CTAs with pages.
 // n_wide / n_narrow: the plan's merge-list counts; pre_w / pre_n: the merge-list
 // entries of this CTA's first wide unit and this warp's first narrow unit, loaded
 // before the grid barrier.
 template <int D, int NWARP>
-SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int warp, int lane, int n_wide, int n_narrow,
+SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int cta, int warp, int lane, int n_wide, int n_narrow,
                          int n_ctas, const GroupInfo& pre_w, const GroupInfo& pre_n) {
   constexpr int NQ = D / 4;     // dim quads
   constexpr int SPW = 32 / NQ;  // split slots per warp
@@ -449,8 +486,8 @@ SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int warp, int la
   };
 
   // wide rows: one CTA each
-  for (int u = blockIdx.x; u < wide_units; u += n_ctas) {
-    const GroupInfo grp = u == static_cast<int>(blockIdx.x) ? pre_w : p.merge_list[u / RU];
+  for (int u = cta; u < wide_units; u += n_ctas) {
+    const GroupInfo grp = u == cta ? pre_w : p.merge_list[u / RU];
     const int r = u % RU;
     if (r >= p.n_rep * grp.nq) continue;  // uniform per CTA
     MergeState st;
@@ -484,7 +521,7 @@ SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int warp, int la
     __syncthreads();
   }
   // narrow rows: one warp each
-  const int u0 = blockIdx.x * NWARP + warp;
+  const int u0 = cta * NWARP + warp;
   for (int u = u0; u < narrow_units; u += n_ctas * NWARP) {
     const GroupInfo grp = u == u0 ? pre_n : p.merge_list[p.max_groups - 1 - u / RU];
     const int r = u % RU;
@@ -518,6 +555,7 @@ SD_DEV bool grid_barrier(PlanHeader* h, unsigned n_ctas, bool wait) {
 }
 
 #include "verify_kernel.cuh"
+static_assert(kTilePages == kPlanTilePages, "the plan and the verify kernel agree on the tile");
 
 // ---------------------------------------------------------------- fp32 contiguous path
 // CUDA-core kernel for the f32 dtype of the reference op (attention.cu:262-272).
