@@ -44,13 +44,16 @@ struct WorkItem {             // 48 bytes
 };
 static_assert(sizeof(WorkItem) == 48, "work item is 48 bytes");
 // What a persistent CTA needs before its first copies: its item range, its first work
-// item and that item's first 32 page ids (0 past the item), one 256-byte line.
+// item and that item's first 32 page ids (0 past the item), and for after its items the
+// merge counts -- one 256-byte line.
 struct CtaDesc {
   WorkItem first;
   int32_t item_begin, item_end;  // the CTA's items: [item_begin, item_end) (every CTA of the grid)
   int32_t pad0[2];
   int32_t pages[32];
-  int32_t pad1[16];
+  // the plan header's merge counts and CTA count, so the merge needs no header load
+  int32_t num_merge_wide, num_merge_narrow, num_ctas;
+  int32_t pad1[13];
 };
 static_assert(sizeof(CtaDesc) == 256, "CTA descriptor is 256 bytes");
 struct GroupInfo {
@@ -351,6 +354,9 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
     const int c = bx - idle;
     p.cdesc[bx].item_begin = c < 0 ? 0 : p.cta_first[c];
     p.cdesc[bx].item_end = c < 0 ? 0 : p.cta_first[c + 1];
+    p.cdesc[bx].num_merge_wide = wcarry;
+    p.cdesc[bx].num_merge_narrow = ncarry;
+    p.cdesc[bx].num_ctas = C;
   }
   // first item and page ids: thread t fills page slot t % 32 of CTA t / 32
   for (int u = threadIdx.x; u < C * 32; u += blockDim.x) {
