@@ -540,9 +540,9 @@ SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int cta, int war
 
 // Grid-wide barrier of the persistent verify kernel: its grid is at most one CTA per
 // SM at one CTA per SM, so every CTA is resident once the kernel's CTAs run.  The
-// arrival counter grows by the grid size per launch (the plan zeroes it): a CTA that
-// arrives as number `old` waits for the counter to reach the next multiple of the
-// grid size.  Only CTAs with merge work wait.  Called by one thread per CTA;
+// arrival counter grows by n_ctas (the CTAs with pages) per launch (the plan zeroes
+// it): a CTA that arrives as number `old` waits for the counter to reach the next
+// multiple of n_ctas.  Only CTAs with merge work wait.  Called by one thread per CTA;
 // bounded: false after ~1 s.
 SD_DEV bool grid_barrier(PlanHeader* h, unsigned n_ctas, bool wait) {
   __threadfence();  // this CTA's partials before its arrival
