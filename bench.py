@@ -135,8 +135,19 @@ def dist_setup():
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
-                                device_id=torch.device("cuda", local))
+        # NCCL prints its version to stdout when the communicator is created: send the
+        # process's stdout to stderr meanwhile, so stdout carries the JSON line only
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                    device_id=torch.device("cuda", local))
+            dist.barrier()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     elif torch.cuda.is_available():
         torch.cuda.set_device(local)
     return world, rank, local
