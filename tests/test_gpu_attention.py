@@ -101,6 +101,31 @@ def test_ragged_decode_rows(fp8, H, D):
     assert_close_attention(got, ref, f"decode rows fp8={fp8} H={H} D={D}")
 
 
+@pytest.mark.parametrize("num_sms", [148, 97, 33, 8, 1])
+@pytest.mark.parametrize("fp8", [False, True])
+def test_grid_sizes(num_sms, fp8):
+    """The same ragged batch on grids of every size: the plan's whole-tile CTA count for small
+    calls with the blocks that get no pages placed first, grids with fewer CTAs than split
+    rows (several merge rounds) and a single CTA that takes every item."""
+    import ctypes
+
+    from specdec_b200 import _lib
+
+    ops = _ops()
+    lens, q_lens = [8192, 3000, 77, 1, 640], [5, 1, 5, 1, 2]
+    cache, ks, vrefs = build_cache(lens, 2, 128, fp8=fp8, seed=41)
+    batch = ops.RaggedBatch.from_lengths(q_lens, lens)
+    g = torch.Generator().manual_seed(43)
+    q = torch.randn(batch.total_rows, 12, 128, generator=g).to(torch.bfloat16)
+    qc = q.cuda()
+    out = torch.empty_like(qc)
+    args = ops.attn_args(qc, out, cache, 0, batch, ops.attn_workspace(batch, 12, cache))
+    args.num_sms = num_sms
+    _lib.check(ops._lib_handle().specdec_paged_attention(ctypes.byref(args), ops._stream()), "paged_attention")
+    torch.cuda.synchronize()
+    assert_close_attention(out.cpu(), oracle_rows(q, ks, vrefs, q_lens), f"num_sms={num_sms} fp8={fp8}")
+
+
 def test_ragged_config4_full_size():
     """The ragged config at its full size (64 sequences, T ~ U[1024, 8192], q_len 1 and 5
     in a 1:1 seeded shuffle, E4M3 V): every output row against the oracle."""
