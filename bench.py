@@ -359,8 +359,10 @@ def measure_e2e(steps, warmup, T=8192, q=5, layers=LAYERS, seed=0):
             dk = din[base + nq:base + nq + nkv].view(q, KV, D)
             dv = din[base + nq + nkv:base + per].view(q, KV, D)
             ops.append_kv(dk, dv, cache, layer, row0=row0, n_new=n_new, pos0=pos0, max_new=q)
+            # the append writes only this step's tokens: the history may be loaded early, as
+            # the engine's decoder does after its append
             ops.paged_attention(dq, cache, layer, batch, out=dout[layer * nq:(layer + 1) * nq].view(q, H, D),
-                                workspace=ws, reuse_plan=True)
+                                workspace=ws, reuse_plan=True, history_ready=layer > 0)
         hout.copy_(dout, non_blocking=True)
 
     step()  # warm the extension outside capture

@@ -38,6 +38,8 @@ struct AppendParams {
 template <int D, bool VF8>
 __global__ void __launch_bounds__(256) append_kernel(const AppendParams p) {
   constexpr int PER = D / 32;  // dims per lane
+  grid_dep_wait();  // launched programmatically: k/v and the lengths may be the preceding work's output
+  grid_dep_launch();
   const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int per_seq = p.max_new * p.KV;
@@ -300,15 +302,9 @@ extern "C" int specdec_append_kv(const SpecdecAppendArgs* a, specdec_stream_t st
   const int64_t blocks = (warps * 32 + 255) / 256;
   if (blocks > 0x7fffffff) return fail(SPECDEC_ERR_INVALID, "append batch too large");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (a->head_dim == 128) {
-    if (vf8)
-      append_kernel<128, true><<<static_cast<unsigned>(blocks), 256, 0, st>>>(p);
-    else
-      append_kernel<128, false><<<static_cast<unsigned>(blocks), 256, 0, st>>>(p);
-  } else {
-    append_kernel<64, false><<<static_cast<unsigned>(blocks), 256, 0, st>>>(p);
-  }
-  return after_launch("append_kernel");
+  auto* kern = a->head_dim == 128 ? (vf8 ? append_kernel<128, true> : append_kernel<128, false>)
+                                  : append_kernel<64, false>;
+  return launch_pdl("append_kernel", kern, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st, p);
 }
 
 extern "C" int specdec_rope_append(const SpecdecRopeAppendArgs* a, specdec_stream_t stream) {
