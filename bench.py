@@ -45,8 +45,8 @@ H, KV, D = 12, 2, 128
 LAYERS = 28
 PAGE = 16
 # DRAM bytes (read + write) of one verify-kernel launch of the headline workload, from an
-# `ncu --set full` capture of `bench.py --profile-case verify8k` (8,648,192 read + 0 written)
-NCU_TRAFFIC_VERIFY8K = 8648192
+# `ncu --set full` capture of `bench.py --profile-case verify8k` (8,649,472 read + 0 written)
+NCU_TRAFFIC_VERIFY8K = 8649472
 
 
 def attn_bytes(T: int, q: int, fp8: bool, heads: int = H, d: int = D) -> float:
