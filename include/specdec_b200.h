@@ -163,7 +163,9 @@ int specdec_paged_attention(const SpecdecAttnArgs* args, specdec_stream_t stream
  *   - A batch needing more than 32 MiB of scratch (see specdec_attn_workspace_bytes)
  *     is rejected with SPECDEC_ERR_WORKSPACE before anything is launched.
  *   - The first call on a device looks up the scratch's device address with that
- *     device current; make that first call before any stream capture.
+ *     device current; make that first call before any stream capture.  The address
+ *     is cached per device and CUDA context: the first call in a new context (after
+ *     cudaDeviceReset, say) looks it up again, so make that call outside capture too.
  *   - All calls share the one scratch area, which keeps the previous call's
  *     contents (nothing in it needs to start at zero).  Calls whose kernels
  *     overlap on the GPU (different streams, or different host threads) race on
@@ -306,6 +308,17 @@ int specdec_gather4_selftest(const void* big, const void* small, int64_t n_rows,
                              int32_t* status, specdec_stream_t stream);
 int specdec_umma_selftest(const void* k, const void* q, const void* v, const void* p, float* out1, float* out2,
                           int32_t* status, specdec_stream_t stream);
+/* Bounded-wait self-check (no counterpart in the reference): every device wait of this
+   library gives up after a time limit, raises SPECDEC_STATUS_TIMEOUT and returns.  This
+   entry point runs those waits with a short limit `limit_ns` (1 us .. 100 ms) where nothing
+   can complete them, so the timeout path itself can be tested:
+     mode 0: one CTA waits on an mbarrier that nothing arrives on (grid must be 1);
+     mode 1: `grid` CTAs (1 .. 8) meet at the grid barrier of the verify kernel expecting
+             `n_ctas` arrivals on the zeroed device u64 `counter` (n_ctas > grid times out,
+             n_ctas == grid passes).
+   waited_ns (device u64, may be NULL) receives the time CTA 0 spent in its wait. */
+int specdec_wait_selftest(int32_t mode, void* counter, int32_t n_ctas, int32_t grid, int64_t limit_ns,
+                          int32_t* status, void* waited_ns, specdec_stream_t stream);
 const char* specdec_last_error(void);
 int specdec_abi_version(void);
 /* Number of kernels this library launched since load (all entry points). */

@@ -98,11 +98,10 @@ __global__ void __launch_bounds__(256) append_kernel(const AppendParams p) {
     for (int e = 0; e < PER; ++e) x[e] = __bfloat162float(p.v_new[src + d0 + e]);
     float m = 0.f;
 #pragma unroll
-    for (int e = 0; e < PER; ++e) m = fmaxf(m, fabsf(x[e]));
+    for (int e = 0; e < PER; ++e) m = amax_nan(m, fabsf(x[e]));
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float s = __fdiv_rn(m, kE4M3Max);
-    if (s == 0.f) s = 1.f;
+    for (int o = 16; o > 0; o >>= 1) m = amax_nan(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = e4m3_scale(m);
     // natural [16 tokens][D] code rows: each lane writes its 4 codes as one word
     uint8_t* vrow = p.v_pool + ph * (D * 16) + slot * D;
     uint32_t word = 0;
@@ -232,11 +231,10 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const RopeAppendParams
     for (int e = 0; e < PER; ++e) x[e] = __bfloat162float(vsrc[d0 + e]);
     float m = 0.f;
 #pragma unroll
-    for (int e = 0; e < PER; ++e) m = fmaxf(m, fabsf(x[e]));
+    for (int e = 0; e < PER; ++e) m = amax_nan(m, fabsf(x[e]));
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float s = __fdiv_rn(m, kE4M3Max);
-    if (s == 0.f) s = 1.f;
+    for (int o = 16; o > 0; o >>= 1) m = amax_nan(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = e4m3_scale(m);
     uint8_t* vrow = p.v_pool + ph * (D * 16) + slot * D;
     uint32_t word = 0;
 #pragma unroll

@@ -37,6 +37,9 @@ SD_DEV float round_to(float v) {
   return to_f<T>(from_f<T>(v));
 }
 
+// torch's CPU rsqrt: 1 / sqrt(x), both steps correctly rounded (rsqrtf is approximate)
+SD_DEV float inv_sqrt_rn(float x) { return __fdiv_rn(1.f, __fsqrt_rn(x)); }
+
 template <typename T>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                       T* __restrict__ y, int hidden, float eps) {
@@ -57,7 +60,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, c
   if (threadIdx.x == 0) {
     float t = 0.f;
     for (int k = 0; k < (blockDim.x >> 5); ++k) t += s_part[k];
-    s_inv = rsqrtf(t / static_cast<float>(hidden) + eps);
+    s_inv = inv_sqrt_rn(t / static_cast<float>(hidden) + eps);
   }
   __syncthreads();
   const float inv = s_inv;
@@ -98,7 +101,7 @@ __global__ void __launch_bounds__(256) rmsnorm_warp_kernel(const __nv_bfloat16* 
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float inv = rsqrtf(ss / static_cast<float>(hidden) + eps);
+  const float inv = inv_sqrt_rn(ss / static_cast<float>(hidden) + eps);
   const uint4* wr = reinterpret_cast<const uint4*>(w);
   uint4* yr = reinterpret_cast<uint4*>(y + row * hidden);
 #pragma unroll

@@ -543,18 +543,18 @@ SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int cta, int war
 // arrival counter grows by n_ctas (the CTAs with pages) per launch (the plan zeroes
 // it): a CTA that arrives as number `old` waits for the counter to reach the next
 // multiple of n_ctas.  Only CTAs with merge work wait.  Called by one thread per CTA;
-// bounded: false after ~1 s.
-SD_DEV bool grid_barrier(PlanHeader* h, unsigned n_ctas, bool wait) {
+// bounded: false after `limit_ns` (~1 s by default).
+SD_DEV bool grid_barrier(unsigned long long* counter, unsigned n_ctas, bool wait, uint64_t limit_ns = kWaitLimitNs) {
   __threadfence();  // this CTA's partials before its arrival
-  const unsigned long long old = atomicAdd(&h->bar_arrive, 1ull);
+  const unsigned long long old = atomicAdd(counter, 1ull);
   if (!wait) return true;
   const unsigned long long target = (old / n_ctas + 1) * n_ctas;
   const uint64_t t0 = globaltimer_ns();
   for (;;) {
     unsigned long long now;
-    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(now) : "l"(&h->bar_arrive) : "memory");
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(now) : "l"(counter) : "memory");
     if (now >= target) break;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
     __nanosleep(64);
   }
   return true;
@@ -957,21 +957,43 @@ constexpr size_t kStaticScratchBytes = size_t(32) << 20;
 static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
 
 // Host code cannot use g_static_scratch's name as a device address (on the host it
-// is only a stand-in symbol).  The device address is looked up once per device,
-// with that device current, and cached.
+// is only a stand-in symbol).  The device address is looked up once per device, with
+// that device current, and cached together with the CUDA context it belongs to: a call
+// made in another context on the same device (after cudaDeviceReset, or from a caller
+// that manages its own contexts) looks the address up again instead of using a stale one.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+static CUcontext current_context() {
+  static CtxGetCurrentFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult qres;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &qres) == cudaSuccess &&
+        qres == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(ptr);
+  }
+  CUcontext ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != CUDA_SUCCESS) return nullptr;
+  return ctx;
+}
+
 static int static_scratch(void** out) {
   static std::mutex mu;
   static void* addr[64] = {};
+  static CUcontext owner[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return fail(SPECDEC_ERR_CUDA, "no current CUDA device for the static scratch");
+  const CUcontext ctx = current_context();  // NULL before the runtime's first use of the device
   std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
+  if (addr[dev] == nullptr || ctx == nullptr || owner[dev] != ctx) {
     void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);  // makes the context current if needed
     if (e != cudaSuccess || p == nullptr)
       return fail(SPECDEC_ERR_CUDA, "cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(e));
     addr[dev] = p;
+    owner[dev] = current_context();
   }
   *out = addr[dev];
   return SPECDEC_OK;
@@ -1107,4 +1129,48 @@ extern "C" int specdec_gather4_selftest(const void* big, const void* small, int6
   sd::gather4_selftest_kernel<<<1, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       mb, ms, make_int4(rows[0], rows[1], rows[2], rows[3]), static_cast<uint8_t*>(out), status);
   return after_launch("gather4_selftest_kernel");
+}
+
+// ---------------------------------------------------------------- bounded-wait self-check
+// Exercises the two waits every kernel of this library relies on with a short limit:
+// mode 0 waits on an mbarrier that nothing arrives on (mbar_wait), mode 1 meets at the
+// grid barrier with `n_ctas` arrivals expected from a grid of `grid` CTAs (grid_barrier).
+// A wait that gives up raises SPECDEC_STATUS_TIMEOUT and the kernel returns; the time the
+// first CTA spent waiting goes to *waited_ns.
+namespace sd {
+__global__ void __launch_bounds__(32) wait_selftest_kernel(int mode, unsigned long long* counter, unsigned n_ctas,
+                                                           uint64_t limit_ns, int32_t* status,
+                                                           unsigned long long* waited_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+  const uint64_t t0 = globaltimer_ns();
+  bool ok = true;
+  if (mode == 0) {
+    ok = __all_sync(0xffffffffu, mbar_wait(&bar, 0, limit_ns));
+  } else if (threadIdx.x == 0) {
+    ok = grid_barrier(counter, n_ctas, true, limit_ns);
+  }
+  if (threadIdx.x == 0) {
+    if (!ok) raise_status(status, SPECDEC_STATUS_TIMEOUT);
+    if (blockIdx.x == 0 && waited_ns != nullptr) *waited_ns = globaltimer_ns() - t0;
+  }
+}
+}  // namespace sd
+
+extern "C" int specdec_wait_selftest(int32_t mode, void* counter, int32_t n_ctas, int32_t grid, int64_t limit_ns,
+                                     int32_t* status, void* waited_ns, specdec_stream_t stream) {
+  if (mode != 0 && mode != 1) return fail(SPECDEC_ERR_INVALID, "wait self-test mode must be 0 or 1");
+  if (limit_ns < 1000 || limit_ns > 100000000) return fail(SPECDEC_ERR_INVALID, "wait limit must be 1 us .. 100 ms");
+  if (grid < 1 || grid > 8) return fail(SPECDEC_ERR_INVALID, "wait self-test grid must be 1 .. 8 CTAs");
+  if (mode == 1 && (counter == nullptr || n_ctas < 1))
+    return fail(SPECDEC_ERR_INVALID, "grid-barrier self-test needs a zeroed device counter and n_ctas >= 1");
+  if (mode == 0 && grid != 1) return fail(SPECDEC_ERR_INVALID, "mbarrier self-test runs one CTA");
+  sd::wait_selftest_kernel<<<grid, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      mode, static_cast<unsigned long long*>(counter), static_cast<unsigned>(n_ctas),
+      static_cast<uint64_t>(limit_ns), status, static_cast<unsigned long long*>(waited_ns));
+  return after_launch("wait_selftest_kernel");
 }

@@ -1,6 +1,6 @@
 // sd_common.cuh -- sm_100a building blocks shared by the kernels of this library:
-// mbarrier / bulk-TMA wrappers, warp-level tensor-core MMA and ldmatrix, FP8
-// conversions, and the page-block layout of the paged KV pool.
+// mbarrier / bulk-TMA wrappers, FP8 conversions, and the page-block layout of the
+// paged KV pool.
 #pragma once
 
 #include <cuda.h>
@@ -82,16 +82,16 @@ SD_DEV uint64_t globaltimer_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Bounded wait for phase `parity` of `bar`.  Gives up after ~1 s of wall time
-// (checked every 256 polls) and returns false; callers then raise
+// Bounded wait for phase `parity` of `bar`.  Gives up after `limit_ns` of wall time
+// (~1 s by default; checked every 256 polls) and returns false; callers then raise
 // SPECDEC_STATUS_TIMEOUT and leave, so a lost arrival can never hang the GPU.
 constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;
-SD_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
+SD_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if ((it & 255u) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
   }
 }
 
@@ -143,32 +143,6 @@ SD_DEV void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// ---------------------------------------------------------------- warp MMA (m16n8k16, fp32 accumulate)
-SD_DEV void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-SD_DEV void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-SD_DEV void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-SD_DEV void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
 // ---------------------------------------------------------------- packing / conversion
 SD_DEV uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);  // .x = lo (low 16 bits)
@@ -192,6 +166,18 @@ SD_DEV uint32_t f32x2_to_e4m3x2(float first, float second) {
   uint16_t r;
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(second), "f"(first));
   return r;
+}
+// Max of two magnitudes (>= 0 or NaN) that keeps a NaN, as torch's amax does (fmaxf drops it):
+// a NaN anywhere in a V row makes the row's scale NaN, and with it every code of the row.
+SD_DEV float amax_nan(float a, float b) { return (b > a || b != b) ? b : a; }
+// Per-token E4M3 scale of quantize_kv_fp8: s = amax / 448 with IEEE division, 1 for an all-zero
+// row; a NaN amax is passed through unchanged (the reference's division returns its NaN
+// operand, the quiet NaN 0x7FC00000 of |NaN|, where the GPU's division would return its own
+// canonical NaN pattern).
+SD_DEV float e4m3_scale(float amax) {
+  if (amax != amax) return amax;
+  const float s = __fdiv_rn(amax, kE4M3Max);
+  return s == 0.f ? 1.f : s;
 }
 SD_DEV float fast_exp2(float x) {
   float y;

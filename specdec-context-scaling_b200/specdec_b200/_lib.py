@@ -181,6 +181,7 @@ SIGNATURES = {
     "specdec_swiglu_packed": (ctypes.c_int, [_vp, _vp, _i64, _i64, _vp]),
     "specdec_umma_selftest": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "specdec_gather4_selftest": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp]),
+    "specdec_wait_selftest": (ctypes.c_int, [_i32, _vp, _i32, _i32, _i64, _vp, _vp, _vp]),
     "specdec_last_error": (ctypes.c_char_p, []),
     "specdec_abi_version": (ctypes.c_int, []),
     "specdec_launch_count": (_i64, []),

@@ -57,6 +57,15 @@ def max_over_ranks(x: float, world: int, device) -> float:
     return float(t.item())
 
 
+def check_shardable(total_seqs: int, world: int) -> None:
+    """Every rank must get at least one sequence: an empty shard cannot build its engine,
+    and a rank that fails alone would leave the others waiting in the final collectives.
+    The check depends only on arguments every rank shares, so all ranks raise together,
+    before any collective."""
+    if total_seqs < world:
+        raise ValueError(f"{total_seqs} sequences cannot be sharded over {world} ranks (at least one per rank)")
+
+
 @dataclass
 class DPResult:
     tokens: torch.Tensor      # (total, max_new): gathered from every rank
@@ -75,6 +84,7 @@ def run_specdec_dp(target_cfg, draft_cfg, *, total_seqs: int, prompt_len: int, m
     from .model import PagedModel
     from .specdec import SpecDecEngine
 
+    check_shardable(total_seqs, world)
     dev = torch.device("cuda", torch.cuda.current_device())
     s, e = shard_bounds(total_seqs, world, rank)
     prompts = synthetic_prompts(total_seqs, prompt_len, target_cfg.vocab, seed)[s:e].to(dev)

@@ -9,10 +9,11 @@ new K/V rows are appended in place instead of re-concatenating the history.
 Per layer of a decode / verify step (rows = packed query rows of all sequences):
   h   = rmsnorm(x)                                 specdec_rmsnorm
   qkv = h W_qkv^T + b_qkv                          cuBLAS (one fused GEMM)
-  q,k = rope(q), rope(k) at each row's position     specdec_apply_rope
-  append k, v (V quantised to E4M3 for an e4m3 cache)      specdec_append_kv
+  q = rope(q) out; rope(k) and v appended to the layer's pages (V quantised to E4M3
+      for an e4m3 cache), one launch                specdec_rope_append
   o   = paged attention of q over the layer's pages        specdec_paged_attention
-  x  += o W_o^T ; x += W_down swiglu(W_gate h2, W_up h2)   cuBLAS + specdec_swiglu
+  x  += o W_o^T                                    cuBLAS (residual added in place)
+  x  += W_down swiglu(W_gate|up rmsnorm(x))        specdec_rmsnorm, cuBLAS, specdec_swiglu_packed
 Prefill (the whole prompt at once) uses torch's fused causal attention for the
 prompt block and appends the prompt's K/V into the pages; decode never does.
 

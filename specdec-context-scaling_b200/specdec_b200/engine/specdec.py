@@ -15,6 +15,11 @@ cache.  One round:
   4. rollback on the device: the target keeps pending + c1 .. cm
      (len + 1 + m), the draft the same minus ck when m == k.
 
+A sequence that has emitted max_new tokens is frozen on the device at the start of
+the next round: its query lengths are 0 in every step of the round (no append, no
+attention rows), accept treats it as inactive (m = 0, lengths kept), and nothing is
+emitted for it, so its caches stop growing while slower sequences finish.
+
 Every step of a round is a fixed-shape device computation (the ragged q_len of
 step 1 lives in device arrays), so a round is captured once in a CUDA graph and
 replayed with no host synchronisation; the host only checks the emitted-token
@@ -42,8 +47,9 @@ class SpecDecEngine:
         self.check_every = check_every
         dev = target.device
         self.device = dev
-        # a round past max_new adds at most k + 1 tokens; the host looks every check_every rounds
-        cap = prompt_len + max_new + (k + 1) * (check_every + 2) + 2
+        # a sequence is frozen once it has max_new tokens, so its caches hold at most the
+        # prompt, max_new + k emitted tokens and one verify block
+        cap = prompt_len + max_new + 2 * (k + 1) + 2
         self.tc = target.new_cache(num_seqs, cap, target_v)
         self.dc = draft.new_cache(num_seqs, cap, draft_v)
         self.L0 = StepLayout(num_seqs, 2, dev)
@@ -58,7 +64,7 @@ class SpecDecEngine:
         self.c_last = torch.zeros(num_seqs, **i32)
         self.cands = torch.zeros(num_seqs, k, **i32)
         self.kp = torch.full((num_seqs,), k, **i32)
-        self.width = max_new + (k + 1) * (check_every + 2)
+        self.width = max_new + k + 1
         self.out = torch.zeros(num_seqs, self.width, **i32)
         self.n_out = torch.zeros(num_seqs, **i32)
         self.g = torch.zeros(num_seqs, k + 1, **i32)
@@ -72,6 +78,7 @@ class SpecDecEngine:
         self.acc_ws = ops.accept_workspace(num_seqs, k + 1, target.cfg.vocab, dev)
         self.graph = None
         self.idx = torch.arange(k + 1, device=dev, dtype=torch.int32)
+        self.active = torch.ones(num_seqs, **i32)   # 0: the sequence has its max_new tokens
 
     # ------------------------------------------------------------------ prompt
     @torch.inference_mode()
@@ -89,6 +96,7 @@ class SpecDecEngine:
         self.out.zero_()
         self.out[:, 0] = self.pending
         self.n_out.fill_(1)
+        self.active.fill_(1)
         self.catch.zero_()
         self.accepted.zero_()
         self.rounds = 0
@@ -97,8 +105,10 @@ class SpecDecEngine:
     def _round(self) -> None:
         k = self.k
         draft, target = self.draft, self.target
+        act = self.active
+        act.copy_(self.n_out < self.max_new)  # frozen sequences: every q_len 0 below
         # 1. draft: [ck_prev, pending] after a full accept, else [pending]
-        q0 = 1 + self.catch
+        q0 = (1 + self.catch) * act
         first = torch.where(self.catch > 0, self.c_last, self.pending)
         tok0 = torch.stack([first, self.pending], dim=1).reshape(-1)
         self.L0.set(self.dc.lengths, q0)
@@ -106,13 +116,13 @@ class SpecDecEngine:
         self.cands[:, 0] = draft.logits(h[self.L0.last_rows()]).argmax(-1).int()
         self.dc.lengths.add_(q0)
         for i in range(1, k):
-            self.L1.set(self.dc.lengths)
+            self.L1.set(self.dc.lengths, act)
             h = draft.step(self.cands[:, i - 1], self.L1, self.dc, self.ws1, status=self.status)
             self.cands[:, i] = draft.logits(h).argmax(-1).int()
-            self.dc.lengths.add_(1)
+            self.dc.lengths.add_(act)
         # 2. target verify of [pending, c1 .. ck]
         vt = torch.cat([self.pending.unsqueeze(1), self.cands], dim=1).reshape(-1)
-        self.LV.set(self.tc.lengths)
+        self.LV.set(self.tc.lengths, act * (k + 1))
         h = target.step(vt, self.LV, self.tc, self.wsv, status=self.status)
         logits = target.logits(h)
         # 3. greedy accept (+ the target's rolled-back length len + 1 + m)
@@ -125,18 +135,18 @@ class SpecDecEngine:
         vals = torch.where(self.idx[:k].unsqueeze(0) < m, self.cands, self.next_token.unsqueeze(1))
         vals = torch.cat([vals, self.next_token.unsqueeze(1)], dim=1)
         pos = (self.n_out.unsqueeze(1) + self.idx.unsqueeze(0)).clamp(max=self.width - 1).long()
-        keep = self.idx.unsqueeze(0) <= m
+        keep = (self.idx.unsqueeze(0) <= m) & (act.unsqueeze(1) > 0)
         self.out.scatter_(1, pos, torch.where(keep, vals, self.out.gather(1, pos)))
-        self.n_out.add_(self.m + 1)
-        self.accepted.add_(self.m)
-        # 4. rollback on the device
+        self.n_out.add_((self.m + 1) * act)
+        self.accepted.add_(self.m)  # 0 for frozen sequences
+        # 4. rollback on the device (accept keeps a frozen sequence's target length)
         self.tc.lengths.copy_(self.new_tlen)
-        full = (self.m == k).int()
-        torch.sub(self.new_tlen, full, out=self.new_dlen)
+        full = (self.m == k).int() * act
+        torch.where(act > 0, self.new_tlen - full, self.dc.lengths, out=self.new_dlen)
         ops.trim_lengths(self.dc.lengths, self.new_dlen, out=self.dc.lengths, status=self.status)
-        self.catch.copy_(full)
-        self.c_last.copy_(self.cands[:, k - 1])
-        self.pending.copy_(self.next_token)
+        torch.where(act > 0, full, self.catch, out=self.catch)
+        torch.where(act > 0, self.cands[:, k - 1], self.c_last, out=self.c_last)
+        torch.where(act > 0, self.next_token, self.pending, out=self.pending)
 
     @torch.inference_mode()
     def capture(self) -> None:
@@ -183,5 +193,6 @@ class SpecDecEngine:
         return self.out[:, :self.max_new]
 
     def acceptance(self) -> float:
-        """Mean accepted candidates per round and sequence."""
+        """Mean accepted candidates per round and sequence (the rounds a sequence was frozen
+        for count as rounds with nothing accepted)."""
         return float(self.accepted.sum()) / max(1, self.rounds * self.B)

@@ -5,11 +5,13 @@ Run in a checkout that has the reference repository importable:
     REFERENCE_ROOT=/path/to/SpecDec-Context-Scaling python tests/golden/make_golden.py
 
 It imports the reference's own functions (specdec.kernels.reference.attention /
-attention_fp32, specdec.engine.model_self.quantize_kv_fp8 / dequantize_kv_fp8,
-specdec.engine.spec_cache, specdec.engine.spec_dec.spec_decode_greedy and
+attention_fp32 / rmsnorm / apply_rope / swiglu, specdec.engine.model_self.quantize_kv_fp8 /
+dequantize_kv_fp8 / QwenLM, specdec.engine.spec_cache,
+specdec.engine.spec_dec.spec_decode_greedy and
 experiments.execution_optimization.fast_spec_dec.spec_decode_greedy_optimized)
 on seeded synthetic inputs and stores inputs and outputs in golden_v1.pt.
 The GPU box never needs the reference: tests compare against this file.
+REFERENCE_ROOT must be set; there is no default location.
 """
 
 from __future__ import annotations
@@ -21,12 +23,12 @@ from pathlib import Path
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
+REF = Path(os.environ["REFERENCE_ROOT"]) if os.environ.get("REFERENCE_ROOT") else None
 
 
 def _import_reference():
-    if not (REF / "specdec").exists():
-        raise SystemExit(f"reference not found at {REF}")
+    if REF is None or not (REF / "specdec").exists():
+        raise SystemExit(f"set REFERENCE_ROOT to a checkout of the reference (got {REF})")
     sys.path.insert(0, str(REF))
     from specdec.kernels import reference as kref  # noqa: E402
     from specdec.engine import model_self, spec_cache, spec_dec  # noqa: E402
@@ -75,8 +77,13 @@ def fp8_cases(model_self):
     edge[0, 1, 4] = 65504.0 * torch.sign(torch.arange(128) - 63.5)
     edge[0, 1, 5] = torch.randn(128, generator=g) * 1e-3
     edge = edge.to(torch.bfloat16)
+    # a NaN in a V row: the reference's amax propagates it, so that row's scale and every
+    # code of the row are NaN
+    nan_rows = torch.randn(1, 2, 3, 128, generator=g)
+    nan_rows[0, 1, 1, 17] = float("nan")
+    nan_rows = nan_rows.to(torch.bfloat16)
     res = {}
-    for name, x in (("outlier", v), ("edge", edge)):
+    for name, x in (("outlier", v), ("edge", edge), ("nan_row", nan_rows)):
         qv, sv = model_self.quantize_kv_fp8(x, model_self.GROUP_V)
         deq = model_self.dequantize_kv_fp8(qv, sv, torch.bfloat16)
         res[name] = dict(x=x, codes=qv.view(torch.uint8).clone(), scale=sv.clone(), deq=deq)
@@ -175,6 +182,79 @@ class ToyLM(torch.nn.Module):
         return (logits if need_logits else None), cache
 
 
+def elementwise_cases(kref):
+    """reference.rmsnorm / apply_rope / swiglu (specdec/kernels/reference.py:14-31) at bf16 and
+    fp32, on the engine's shapes: hidden 1536 and 896 rows, (B, H, S, 128) and (B, H, S, 64)
+    rotary inputs with the engine's cos / sin tables, and the FFN widths 8960 and 4864."""
+    out = {}
+    for dt_name, dt in (("bf16", torch.bfloat16), ("f32", torch.float32)):
+        g = torch.Generator().manual_seed(300 if dt is torch.bfloat16 else 301)
+        for hidden in (1536, 896, 1000):
+            x = (torch.randn(13, hidden, generator=g) * 3.0).to(dt)
+            w = torch.randn(hidden, generator=g).to(dt)
+            out[f"rmsnorm_{dt_name}_{hidden}"] = dict(x=x, w=w, out=kref.rmsnorm(x, w))
+        for H, S, D in ((12, 5, 128), (14, 2, 64), (2, 9, 128)):
+            x = torch.randn(1, H, S, D, generator=g).to(dt)
+            pos = torch.arange(8190, 8190 + S, dtype=torch.float32)
+            inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, dtype=torch.float32) / D))
+            ang = torch.outer(pos, inv)
+            cos = torch.cat([ang.cos(), ang.cos()], -1)[None, None].to(dt)
+            sin = torch.cat([ang.sin(), ang.sin()], -1)[None, None].to(dt)
+            out[f"rope_{dt_name}_{H}x{S}x{D}"] = dict(x=x, cos=cos, sin=sin, out=kref.apply_rope(x, cos, sin))
+        for inter in (8960, 4864):
+            gate = (torch.randn(3, inter, generator=g) * 2.0).to(dt)
+            up = torch.randn(3, inter, generator=g).to(dt)
+            out[f"swiglu_{dt_name}_{inter}"] = dict(gate=gate, up=up, out=kref.swiglu(gate, up))
+    return out
+
+
+def model_cases(model_self):
+    """A tiny random-init reference QwenLM (model_self.py:835-931) in bf16 on the CPU: the
+    target geometry's heads (12 query : 2 KV heads, head_dim 128) at width 128, 2 layers,
+    Qwen2 q/k/v biases.  For the bf16 ("fp16") and V-only FP8 ("v_fp8") cache formats: the
+    prompt pass's last-row logits, the logits of a 5-token verify block on top of the prompt,
+    and 6 greedy tokens decoded one at a time from the prompt (QwenLM._run with dict caches),
+    with the weights as a state dict."""
+    torch.manual_seed(123)
+    m = model_self.QwenLM(vocab_size=512, hidden=128, heads=12, kv_heads=2, head_dim=128, intermediate=256,
+                          num_layers=2, rope_theta=1_000_000.0, rms_eps=1e-6, attn_bias=True)
+    # the constructor's own seeded init, rescaled so that greedy decoding does not just repeat
+    # the last token (tied embeddings at N(0,1) dominate the residual stream), and norm
+    # weights that are not all ones
+    with torch.no_grad():
+        for name, p in m.named_parameters():
+            if "norm" in name:
+                p.copy_(1.0 + 0.1 * torch.randn_like(p))
+            elif "embed" in name:
+                p.mul_(0.05)
+            else:
+                p.mul_(3.0)
+    m = m.to(torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(124)
+    prompt = torch.randint(0, 512, (1, 37), generator=g)
+    block = torch.randint(0, 512, (1, 5), generator=g)
+    res = dict(config=dict(vocab=512, hidden=128, heads=12, kv_heads=2, head_dim=128, intermediate=256, layers=2,
+                           rope_theta=1_000_000.0, eps=1e-6, attn_bias=True),
+               state={k: v.clone() for k, v in m.state_dict().items()}, prompt=prompt, block=block)
+    with torch.no_grad():
+        for fmt in ("fp16", "v_fp8"):
+            m.set_kv_format(fmt)
+            lg, cache = m._run(m.embed_tokens(prompt), None)
+            prompt_logits = lg[0, -1].clone()
+            vb, _ = m._run(m.embed_tokens(block), cache)
+            # greedy decode from a fresh prompt pass
+            lg, cache = m._run(m.embed_tokens(prompt), None)
+            toks, step_logits = [], []
+            for _ in range(6):
+                t = int(lg[0, -1].argmax())
+                toks.append(t)
+                step_logits.append(lg[0, -1].clone())
+                lg, cache = m._run(m.embed_tokens(torch.tensor([[t]])), cache)
+            res[fmt] = dict(prompt_logits=prompt_logits, verify_logits=vb[0].clone(), greedy=toks,
+                            greedy_logits=torch.stack(step_logits))
+    return res
+
+
 def executor_traces(spec_dec, fast_spec_dec):
     traces = []
     for seed, noise, max_new in [(1, 0.0, 13), (2, 0.3, 16), (3, 1.5, 12), (4, 0.8, 17)]:
@@ -203,6 +283,8 @@ def main():
         spec_cache=spec_cache_cases(spec_cache),
         accept=accept_cases(),
         traces=executor_traces(spec_dec, fast_spec_dec),
+        elementwise=elementwise_cases(kref),
+        model=model_cases(model_self),
     )
     path = HERE / "golden_v1.pt"
     torch.save(data, path)

@@ -109,3 +109,12 @@ def test_ops_reject_other_backends():
         with pytest.raises(ValueError):
             ops.rmsnorm(x, x[0], backend=backend)
     assert ops.triton_available() is False
+
+
+def test_wait_selftest_rejects_bad_arguments_without_a_device(lib):
+    from specdec_b200 import _lib
+
+    assert lib.specdec_wait_selftest(2, None, 1, 1, 1_000_000, None, None, None) == _lib.ERR_INVALID
+    assert lib.specdec_wait_selftest(0, None, 1, 1, 10 ** 10, None, None, None) == _lib.ERR_INVALID
+    assert lib.specdec_wait_selftest(1, None, 1, 1, 1_000_000, None, None, None) == _lib.ERR_INVALID
+    assert lib.specdec_wait_selftest(0, None, 1, 2, 1_000_000, None, None, None) == _lib.ERR_INVALID

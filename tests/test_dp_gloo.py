@@ -11,7 +11,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from specdec_b200.engine.dp import gather_rows, max_over_ranks, shard_bounds, synthetic_prompts
+from specdec_b200.engine.dp import check_shardable, gather_rows, max_over_ranks, shard_bounds, synthetic_prompts
 
 
 @pytest.mark.parametrize("total,world", [(256, 1), (256, 2), (256, 8), (10, 3), (3, 4), (0, 2)])
@@ -30,6 +30,13 @@ def test_shard_bounds_cover_every_sequence_once(total, world):
 def test_shard_bounds_rejects_bad_rank():
     with pytest.raises(ValueError):
         shard_bounds(8, 2, 2)
+
+
+def test_fewer_sequences_than_ranks_is_rejected_on_every_rank():
+    """An empty shard is refused up front by a check every rank computes alike."""
+    check_shardable(8, 8)
+    with pytest.raises(ValueError):
+        check_shardable(3, 4)
 
 
 def test_synthetic_prompts_are_identical_across_calls():

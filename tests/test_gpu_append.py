@@ -28,6 +28,9 @@ def test_append_matches_oracle_pools(fp8, D):
     cap = 320
     ks_old, vs_old = seeded_kv(before, KV, D, seed=21, fp8=fp8)
     ks_new, vs_new = seeded_kv(n_new, KV, D, seed=22, fp8=fp8)
+    if fp8:
+        # a NaN in one V row: torch's amax keeps it, so that row's scale and codes are NaN
+        vs_new[1][1, 2, 17] = float("nan")
     cache, _ = cache_from_kv(ks_old, vs_old, KV, D, fp8=fp8, seed=23, capacity=cap)
     # packed new rows (rows, KV, D)
     k_rows = torch.cat([k.permute(1, 0, 2) for k in ks_new], dim=0).contiguous().cuda()
@@ -104,9 +107,14 @@ def test_gather_layer_round_trip():
 
 
 @pytest.mark.parametrize("fp8,H,D", [(True, 12, 128), (False, 12, 128), (False, 14, 64)])
-def test_rope_append_equals_rope_then_append(fp8, H, D):
-    """The fused step seam (one launch after the QKV projection) writes the same pool
-    bytes and rotated queries as apply_rope on q and k followed by append_kv."""
+def test_rope_append_matches_oracle(fp8, H, D):
+    """The fused step seam (one launch after the QKV projection) against the oracle: the
+    rotated queries equal reference.apply_rope (specdec/kernels/reference.py:23-27) of q,
+    bit for bit, and the pool holds apply_rope of k and the quantize_kv_fp8 codes and scales
+    of v (model_self.py:304-314) at the appended positions, bit for bit.  The unfused
+    kernels (apply_rope, then append_kv) write the same bytes."""
+    from oracle import elementwise as oel
+    from oracle import fp8 as ofp8
     from specdec_b200.engine.paged_cache import PagedKVCache
 
     ops = _ops()
@@ -115,9 +123,15 @@ def test_rope_append_equals_rope_then_append(fp8, H, D):
     q_len = [5, 1, 3, 5, 0]
     rows = B * qmax
     g = torch.Generator().manual_seed(31)
-    qkv = torch.randn(rows, H + 2 * KV, D, generator=g).to(torch.bfloat16).cuda()
-    cos = torch.randn(rows, D, generator=g).to(torch.bfloat16).cuda()
-    sin = torch.randn(rows, D, generator=g).to(torch.bfloat16).cuda()
+    qkv_h = (torch.randn(rows, H + 2 * KV, D, generator=g) * 2.0).to(torch.bfloat16)
+    # the engine's tables: cos / sin of fp32 angles at each row's position, rounded to bf16
+    pos = torch.tensor([before[r // qmax] + min(r % qmax, max(q_len[r // qmax] - 1, 0)) for r in range(rows)],
+                       dtype=torch.float32)
+    inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, dtype=torch.float32) / D))
+    ang = torch.outer(pos, inv)
+    cos_h = torch.cat([ang.cos(), ang.cos()], -1).to(torch.bfloat16)
+    sin_h = torch.cat([ang.sin(), ang.sin()], -1).to(torch.bfloat16)
+    qkv, cos, sin = qkv_h.cuda(), cos_h.cuda(), sin_h.cuda()
     row0 = torch.arange(B, dtype=torch.int32, device="cuda") * qmax
     nn = torch.tensor(q_len, dtype=torch.int32, device="cuda")
     pos0 = torch.tensor(before, dtype=torch.int32, device="cuda")
@@ -127,15 +141,34 @@ def test_rope_append_equals_rope_then_append(fp8, H, D):
     q_fused = ops.rope_append(qkv, cos, sin, caches[0], 0, num_q_heads=H, row0=row0, n_new=nn, pos0=pos0,
                               max_new=qmax, status=status)
     # unfused: rope of q and k as (1, heads, rows, D) views, then append
-    q_ref = ops.apply_rope(qkv[:, :H].transpose(0, 1).unsqueeze(0), cos, sin)[0].transpose(0, 1)
     k_rot = ops.apply_rope(qkv[:, H:H + KV].transpose(0, 1).unsqueeze(0), cos, sin)[0].transpose(0, 1)
     ops.append_kv(k_rot.contiguous(), qkv[:, H + KV:].contiguous(), caches[1], 0, row0=row0, n_new=nn, pos0=pos0,
                   max_new=qmax, status=status)
     torch.cuda.synchronize()
     assert int(status.item()) == 0
-    assert torch.equal(q_fused, q_ref)
-    a, b = caches[0].pools[0], caches[1].pools[0]
-    assert torch.equal(a.k.view(torch.int16), b.k.view(torch.int16))
-    assert torch.equal(a.v.view(torch.uint8), b.v.view(torch.uint8))
+
+    # oracle: the reference formula on (heads, rows, D) views, per-row cos / sin
+    c4, s4 = cos_h.unsqueeze(0), sin_h.unsqueeze(0)
+    q_ref = oel.apply_rope(qkv_h[:, :H].transpose(0, 1), c4, s4).transpose(0, 1)
+    k_ref = oel.apply_rope(qkv_h[:, H:H + KV].transpose(0, 1), c4, s4)  # (KV, rows, D)
+    v_in = qkv_h[:, H + KV:].transpose(0, 1)                             # (KV, rows, D)
+    assert torch.equal(q_fused.cpu().view(torch.int16), q_ref.contiguous().view(torch.int16))
+    for b in range(B):
+        n = q_len[b]
+        if n == 0:
+            continue
+        sl = slice(b * qmax, b * qmax + n)
+        got = caches[0].gather_layer(0, b, before[b] + n)
+        assert torch.equal(got["k"][0, :, before[b]:].cpu().view(torch.int16), k_ref[:, sl].contiguous().view(torch.int16))
+        if fp8:
+            codes, scale = ofp8.quantize_v(v_in[:, sl].float().numpy())
+            np.testing.assert_array_equal(got["v"][0, :, before[b]:].view(torch.uint8).cpu().numpy(), codes)
+            np.testing.assert_array_equal(got["v_scale"][0, :, before[b]:, 0].cpu().numpy().view(np.uint32),
+                                          scale[..., 0].view(np.uint32))
+        else:
+            assert torch.equal(got["v"][0, :, before[b]:].cpu().view(torch.int16), v_in[:, sl].contiguous().view(torch.int16))
+    a, b2 = caches[0].pools[0], caches[1].pools[0]
+    assert torch.equal(a.k.view(torch.int16), b2.k.view(torch.int16))
+    assert torch.equal(a.v.view(torch.uint8), b2.v.view(torch.uint8))
     if fp8:
-        assert torch.equal(a.v_scale, b.v_scale)
+        assert torch.equal(a.v_scale, b2.v_scale)

@@ -61,7 +61,7 @@ def _paged_case(lens, q_lens, H, KV, D, fp8, seed):
 
 @pytest.mark.parametrize("fp8", [False, True])
 @pytest.mark.parametrize("S", [1, 2, 5])
-@pytest.mark.parametrize("T", [5, 16, 17, 100, 2048, 8192])
+@pytest.mark.parametrize("T", [5, 16, 17, 100, 2048, 4096, 8192])
 def test_paged_attention_single_sequence(fp8, S, T):
     got, ref, *_ = _paged_case([T], [S], 12, 2, 128, fp8, seed=T * 10 + S)
     assert_close_attention(got, ref, f"fp8={fp8} S={S} T={T}")
@@ -140,6 +140,82 @@ def test_ragged_config4_full_size():
     q = torch.randn(batch.total_rows, 12, 128, generator=torch.Generator().manual_seed(11)).to(torch.bfloat16)
     got = ops.paged_attention(q.cuda(), cache, 0, batch).cpu()
     assert_close_attention(got, oracle_rows(q, ks, vrefs, q_lens), "ragged config 4")
+
+
+def test_ragged_config4_verify_accept_trim_cycle():
+    """The ragged config's whole cycle (64 sequences, T ~ U[1024, 8192], q_len 1 and 5 in a
+    1:1 seeded shuffle, E4M3 V), for 4 rounds: append each sequence's q_len new tokens
+    (append_kv: bf16 K, E4M3 V), attention over the grown history, then for every verify
+    row an accepted count m ~ min(Geometric(0.5) - 1, 4) and the device rollback of the
+    rejected tail (trim_lengths to len + 1 + m: the verify block's pending token plus the
+    m accepted candidates, spec_dec.py:235-243); decode rows keep their token.  After every
+    round the lengths, the page table and the FP8 codes / scales and bf16 K of every kept
+    token are bit-exact against the oracle's restatement of the same cycle, and every
+    output row is within the attention tolerance of the oracle's attention."""
+    from oracle import fp8 as ofp8
+
+    ops = _ops()
+    g = torch.Generator().manual_seed(4)
+    lens = [int(x) for x in torch.randint(1024, 8193, (64,), generator=g)]
+    q_lens = [1, 5] * 32
+    perm = torch.randperm(64, generator=g).tolist()
+    q_lens = [q_lens[i] for i in perm]
+    rounds, KV, D, H = 4, 2, 128, 12
+    cache, ks, _ = build_cache(lens, KV, D, fp8=True, seed=4, over_provision=1, capacity=max(lens) + 5 * rounds)
+    # the oracle keeps the bf16 K / V token lists of every sequence
+    from gpu_helpers import seeded_kv
+
+    _, vs = seeded_kv(lens, KV, D, 4, True)
+    ks, vs = list(ks), list(vs)
+    pt0 = cache.page_table.clone()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    batch = None
+    for r in range(rounds):
+        gr = torch.Generator().manual_seed(100 + r)
+        n_rows = sum(q_lens)
+        k_rows = torch.randn(n_rows, KV, D, generator=gr).to(torch.bfloat16)
+        v_rows = torch.from_numpy(ofp8.outlier_v((n_rows, KV, D), 200 + r)).to(torch.bfloat16)
+        row0 = [sum(q_lens[:b]) for b in range(64)]
+        i32 = lambda x: torch.tensor(x, dtype=torch.int32, device="cuda")  # noqa: E731
+        ops.append_kv(k_rows.cuda(), v_rows.cuda(), cache, 0, row0=i32(row0), n_new=i32(q_lens), pos0=i32(lens),
+                      max_new=5, len_out=cache.lengths, status=status)
+        for b in range(64):
+            sl = slice(row0[b], row0[b] + q_lens[b])
+            ks[b] = torch.cat([ks[b], k_rows[sl].transpose(0, 1)], dim=1)
+            vs[b] = torch.cat([vs[b], v_rows[sl].transpose(0, 1)], dim=1)
+        grown = [n + q for n, q in zip(lens, q_lens)]
+        batch = ops.RaggedBatch.from_lengths(q_lens, grown)
+        q = torch.randn(batch.total_rows, H, D, generator=gr).to(torch.bfloat16)
+        got = ops.paged_attention(q.cuda(), cache, 0, batch, status=status).cpu()
+        vrefs = []
+        for v in vs:
+            c, sc = ofp8.quantize_v(v.float().numpy())
+            vrefs.append(torch.from_numpy(ofp8.dequantize_v(c, sc)).to(torch.bfloat16))
+        assert_close_attention(got, oracle_rows(q, ks, vrefs, q_lens), f"cycle round {r}")
+        # accept + rollback of the verify rows
+        m = []
+        for b in range(64):
+            u = torch.rand(1, generator=gr).item()
+            geo = 0
+            while u < 0.5 ** (geo + 1) and geo < 4:  # P(m >= j) = 0.5 ** j, truncated at 4
+                geo += 1
+            m.append(geo)
+        new_len = [n + 1 + mm if q == 5 else n + 1 for n, q, mm in zip(lens, q_lens, m)]
+        ops.trim_lengths(cache.lengths, i32(new_len), out=cache.lengths, status=status)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0, f"round {r}: status {int(status.item()):#x}"
+        lens = new_len
+        ks = [k[:, :n] for k, n in zip(ks, lens)]
+        vs = [v[:, :n] for v, n in zip(vs, lens)]
+        assert cache.lengths.cpu().tolist() == lens
+        assert torch.equal(cache.page_table, pt0)
+        for b in range(0, 64, 7 if r < rounds - 1 else 1):
+            kept = cache.gather_layer(0, b, lens[b])
+            codes, sc = ofp8.quantize_v(vs[b].float().numpy())
+            assert torch.equal(kept["k"][0].cpu().view(torch.int16), ks[b].view(torch.int16)), f"K seq {b} round {r}"
+            assert (kept["v"][0].view(torch.uint8).cpu().numpy() == codes).all(), f"codes seq {b} round {r}"
+            assert (kept["v_scale"][0, :, :, 0].cpu().numpy().view("u4") == sc[..., 0].view("u4")).all(), \
+                f"scales seq {b} round {r}"
 
 
 def test_draft_decode_full_size():

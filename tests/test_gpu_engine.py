@@ -174,3 +174,38 @@ def test_specdec_graph_replay_equals_eager_rounds():
         eng.decode(use_graph=use_graph)
         outs.append(eng.tokens().cpu())
     assert torch.equal(outs[0], outs[1])
+
+
+def test_specdec_mixed_acceptance_freezes_finished_sequences():
+    """A batch whose sequences accept at very different rates: a draft a little off the target
+    (weights + 0.006 N(0,1) noise) on prompts of which half repeat one token.  Sequences that
+    accept every candidate finish in a few rounds and are frozen while the slow ones go on,
+    so the caches (sized for max_new + two verify blocks) never overflow, and every sequence
+    still emits the target's greedy tokens."""
+    from specdec_b200.engine.model import PagedModel, random_state
+    from specdec_b200.engine.specdec import SpecDecEngine
+
+    tcfg, _ = _cfgs()
+    tstate = random_state(tcfg, 21, "cuda", std=0.05)
+    gn = torch.Generator(device="cuda").manual_seed(99)
+    dstate = {k: (v.float() + 0.006 * torch.randn(v.shape, generator=gn, device="cuda")).to(v.dtype)
+              if "norm" not in k else v for k, v in tstate.items()}
+    target, draft = PagedModel(tcfg, tstate), PagedModel(tcfg, dstate)
+    ref = _oracle(tcfg, tstate)
+    B, P, N, k = 8, 48, 24, 4
+    g = torch.Generator().manual_seed(7)
+    prompts = torch.randint(0, tcfg.vocab, (B, P), generator=g, dtype=torch.int32)
+    for b in range(0, B, 2):
+        prompts[b, :] = prompts[b, 0]
+    prompts = prompts.cuda()
+    eng = SpecDecEngine(target, draft, B, P, N, k=k)
+    eng.capture()
+    eng.prefill(prompts)
+    eng.decode()  # raises on a device status (a page overflow among them)
+    got = eng.tokens().cpu()
+    _check_tokens(got, prompts, ref, N)
+    acc = eng.accepted.cpu()
+    # the fastest sequence accepted at least two verify blocks more than the slowest: without
+    # freezing it would have grown past the caches' capacity
+    assert int(acc.max() - acc.min()) >= 2 * (k + 1), acc.tolist()
+    assert int(eng.tc.lengths.max()) <= P + N + 2 * (k + 1)

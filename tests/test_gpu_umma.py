@@ -52,3 +52,30 @@ def test_tma_gather4_page_rows():
         assert int(status.item()) == 0
         assert torch.equal(out[:8192].view(4, 2048).cpu(), big[rows].cpu())
         assert torch.equal(out[8192:].view(4, 64).cpu(), small[rows].cpu())
+
+
+@pytest.mark.parametrize("mode,n_ctas,grid,expect_timeout", [(0, 0, 1, True), (1, 3, 2, True), (1, 2, 2, False)])
+def test_bounded_waits_give_up_and_report(mode, n_ctas, grid, expect_timeout):
+    """The timeout path every device wait of the library relies on, with a 1 ms limit:
+    an mbarrier that nothing arrives on, and the grid barrier expecting more CTAs than the
+    grid has, raise SPECDEC_STATUS_TIMEOUT and return (after about the limit, well before
+    the default one-second limit); a grid barrier whose CTAs all arrive passes."""
+    from specdec_b200 import _lib
+
+    lib = _lib.load_library()
+    counter = torch.zeros(1, dtype=torch.int64, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    waited = torch.zeros(1, dtype=torch.int64, device="cuda")
+    limit = 1_000_000
+    _lib.check(lib.specdec_wait_selftest(mode, counter.data_ptr(), n_ctas, grid, limit, status.data_ptr(),
+                                         waited.data_ptr(), torch.cuda.current_stream().cuda_stream), "wait_selftest")
+    torch.cuda.synchronize()
+    st, ns = int(status.item()), int(waited.item())
+    if expect_timeout:
+        assert st == _lib.STATUS_TIMEOUT
+        assert limit <= ns < 100 * limit
+    else:
+        assert st == 0 and ns < limit
+    # the context is still usable
+    assert float(torch.ones(4, device="cuda").sum()) == 4.0
+

@@ -141,3 +141,52 @@ def test_product_layout_matches_oracle_layout():
     assert pc.vblock_index(128).tolist() == opg.vblock_perm(128).tolist()
     # the bf16 block permutation is a bijection onto the block
     assert sorted(opg.kblock_perm(128).tolist()) == list(range(16 * 128))
+
+
+def test_elementwise_oracle_matches_reference(golden):
+    """oracle/elementwise.py against reference.rmsnorm / apply_rope / swiglu
+    (specdec/kernels/reference.py:14-31): the same torch ops, bit-identical results."""
+    from oracle import elementwise as oel
+
+    cases = golden["elementwise"]
+    assert len(cases) == 16
+    for name, c in cases.items():
+        if name.startswith("rmsnorm"):
+            got = oel.rmsnorm(c["x"], c["w"])
+        elif name.startswith("rope"):
+            got = oel.apply_rope(c["x"], c["cos"], c["sin"])
+        else:
+            got = oel.swiglu(c["gate"], c["up"])
+        assert got.dtype == c["out"].dtype, name
+        assert torch.equal(got, c["out"]), name
+
+
+def _golden_model(golden):
+    import oracle.engine as oeng
+
+    g = golden["model"]
+    c = g["config"]
+    m = oeng.QwenLM(c["vocab"], c["hidden"], c["heads"], c["kv_heads"], c["head_dim"], c["intermediate"], c["layers"],
+                    rope_theta=c["rope_theta"], attn_bias=c["attn_bias"]).to(torch.bfloat16)
+    m.load_state_dict(g["state"], strict=True)
+    return m.eval(), g
+
+
+@pytest.mark.parametrize("fmt", ["fp16", "v_fp8"])
+def test_engine_oracle_matches_reference_model(golden, fmt):
+    """oracle/engine.py (the model-level restatement the engine tests use) against a tiny
+    reference QwenLM (model_self.py:835-931) with the same weights: prompt-pass logits,
+    a 5-token verify block on the prompt's dict cache, and greedy decoding, for the bf16
+    and V-only FP8 cache formats.  Same torch CPU ops: identical bits."""
+    import oracle.engine as oeng
+
+    m, g = _golden_model(golden)
+    m.set_kv_format(fmt)
+    want = g[fmt]
+    with torch.inference_mode():
+        lg, cache = m._run(m.embed_tokens(g["prompt"]), None)
+        assert torch.equal(lg[0, -1], want["prompt_logits"])
+        vb, _ = m._run(m.embed_tokens(g["block"]), cache)
+        assert torch.equal(vb[0], want["verify_logits"])
+        toks, _ = oeng.greedy_decode(m, g["prompt"], len(want["greedy"]))
+    assert toks == want["greedy"]

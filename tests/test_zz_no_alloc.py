@@ -5,8 +5,8 @@ device memory and passes only inputs, outputs and a stream, or an FFI binding
 without a CUDA allocator.  For them the library keeps a 32 MiB scratch array of its
 own.  These tests call that entry point through the C ABI (ctypes) twice in a row,
 on two different batches, and compare each result with the regular entry point
-(caller workspace) under the attention tolerance of the other GPU tests.  The file
-is named to be collected last.
+(caller workspace) under the attention tolerance of the other GPU tests, and with the
+CPU oracle.  The file is named to be collected last.
 """
 
 from __future__ import annotations
@@ -16,7 +16,7 @@ import ctypes
 import pytest
 import torch
 
-from gpu_helpers import ATOL, RTOL, build_cache
+from gpu_helpers import ATOL, RTOL, assert_close_attention, build_cache, oracle_rows
 from oracle import attention as oatt
 
 pytestmark = pytest.mark.gpu
@@ -40,10 +40,10 @@ def _noalloc_call(q, cache, batch):
 def _case(lens, q_lens, fp8, seed):
     from specdec_b200.kernels import ops
 
-    cache, _, _ = build_cache(lens, 2, 128, fp8=fp8, seed=seed)
+    cache, ks, vrefs = build_cache(lens, 2, 128, fp8=fp8, seed=seed)
     batch = ops.RaggedBatch.from_lengths(q_lens, lens)
     q = torch.randn(batch.total_rows, 12, 128, generator=torch.Generator().manual_seed(seed)).to(torch.bfloat16)
-    return cache, batch, q.cuda()
+    return cache, batch, q.cuda(), oracle_rows(q, ks, vrefs, q_lens)
 
 
 def test_noalloc_matches_workspace_entry_two_calls():
@@ -53,12 +53,14 @@ def test_noalloc_matches_workspace_entry_two_calls():
         _case([8192], [5], fp8=True, seed=41),               # batch-1 verify, many splits
         _case([300, 2048, 77, 1500], [1, 5, 5, 1], fp8=False, seed=42),  # ragged mixed rows
     ]
-    for cache, batch, q in cases:
+    for cache, batch, q, ref in cases:
         got = _noalloc_call(q, cache, batch)
         want = ops.paged_attention(q, cache, 0, batch)
         torch.cuda.synchronize()
         ok, err, _ = oatt.within_tolerance(got.cpu(), want.cpu(), RTOL, ATOL)
         assert ok, f"no-alloc output differs from the workspace entry point (max |err| {err:.3e})"
+        # and both against the oracle (the fp32 attention formula on the dequantised history)
+        assert_close_attention(got.cpu(), ref, "no-alloc vs oracle")
 
 
 def test_noalloc_rejects_batches_beyond_the_static_scratch():
