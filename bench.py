@@ -6,18 +6,22 @@ q_len 5 (k = 4 draft tokens + 1 bonus), GQA 12:2, head_dim 128, BF16 K/V in
 16-token pages with a seeded random page order, context 8192.  One step is the
 verify attention of one target forward: 28 layers, each with its own paged cache
 (28 x 8.4 MB = 235 MB of KV per step, larger than the 126 MB L2, so every step
-reads HBM).  The step (device plan + 28 split-KV + 28 merge launches) is a CUDA
-graph replayed K times.
+reads HBM).  The step (device plan + 28 verify launches) is a CUDA graph replayed
+K times; the K-step window is timed 5 times and the median window is reported.
 
   value     algorithmic attention bytes of all ranks / max-over-ranks device time
             (bytes per call = 1024.25 T + 6144 q for bf16 V; 776.25 T + 6144 q for E4M3 V)
   e2e       the same metric through the public API with host buffers: every layer
             copies its q and new K/V rows from pinned host memory, appends them,
             runs paged attention and copies the output back
-  roofline  the split-KV kernel, timed with CUDA events recorded around each of
-            its launches inside the graph, against MEASURED_PEAKS.json hbm_gbs
+  roofline  the verify kernel's in-step duration: a graph of the same step's 28 verify
+            launches without the plan (programmatic dependent launches as in the step),
+            timed with CUDA events over its replays, against MEASURED_PEAKS.json hbm_gbs
   cpu_baseline / --impl reference: the reference's eager attention formula
-            (CPU oracle, torch on all host threads) on the same per-call shape
+            (CPU oracle, torch on all host threads) on the same step (28 layer calls)
+  extras    the other attention configs, the append-quantize kernel, the
+            CPU timings of the FP8 quantiser and of greedy SpecDec, and SpecDec with a
+            draft that always agrees with the target
 
 Multi-GPU (torchrun): every rank runs its own batch-1 workload (weak scaling,
 sequences are independent); no collective in the timed region.
@@ -204,7 +208,7 @@ def filled_cache(num_layers, lens, fp8, seed, d=D):
 class GraphStep:
     """One verify/decode pass over every layer: device plan + per-layer paged attention, in a CUDA graph."""
 
-    def __init__(self, cache, q_lens, ctx_lens, seed=0, events=False, heads=H):
+    def __init__(self, cache, q_lens, ctx_lens, seed=0, events=False, heads=H, with_plan=True):
         import torch
 
         from specdec_b200.kernels import ops
@@ -224,6 +228,8 @@ class GraphStep:
         from specdec_b200 import _lib
 
         self._lib = _lib
+        self.with_plan = with_plan
+        ops.ragged_plan(self.q[0], self.cache, self.batch, self.ws, status=self.status)
         self._run()  # warm the extension (function attributes, plan) outside capture
         torch.cuda.synchronize()
         n0 = _lib.load_library().specdec_launch_count()
@@ -239,12 +245,15 @@ class GraphStep:
     def _run(self):
         from specdec_b200.kernels import ops
 
-        ops.ragged_plan(self.q[0], self.cache, self.batch, self.ws, status=self.status)
+        if self.with_plan:
+            ops.ragged_plan(self.q[0], self.cache, self.batch, self.ws, status=self.status)
         for layer in range(self.cache.num_layers):
-            # layer 0 follows the plan kernel directly; later layers follow attention
-            # kernels, which write no KV, page table or plan: their loads may start early
+            # layer 0 follows the plan kernel directly (or, without the plan, the previous
+            # replay's last attention kernel); later layers follow attention kernels, which
+            # write no KV, page table or plan: their loads may start early
             ops.paged_attention(self.q[layer], self.cache, layer, self.batch, out=self.out[layer], workspace=self.ws,
-                                reuse_plan=True, status=self.status, history_ready=layer > 0,
+                                reuse_plan=True, status=self.status,
+                                history_ready=layer > 0 or not self.with_plan,
                                 split_events=None if self.events is None else self.events[layer])
 
     def replay(self):
@@ -273,6 +282,16 @@ def time_steps(step, steps, warmup, world):
     return t0.elapsed_time(t1)
 
 
+def time_windows(step, steps, warmup, world, windows=5):
+    """W warm-up steps, then `windows` timed windows of exactly `steps` steps each (barrier +
+    synchronize on both sides of every window); returns each window's max-over-ranks ms."""
+    out = []
+    for w in range(windows):
+        ms = time_steps(step, steps, warmup if w == 0 else 0, world)
+        out.append(max_over_ranks(ms, world))
+    return out
+
+
 def measure_config(T, q, fp8, steps, warmup, layers=LAYERS, seed=0):
     """(GB/s, ms/step) of one GPU for a batch-1 q/T config over `layers` distinct caches."""
     import torch
@@ -288,8 +307,9 @@ def measure_config(T, q, fp8, steps, warmup, layers=LAYERS, seed=0):
     return layers * attn_bytes(T, q, fp8) * steps / (ms * 1e-3) / 1e9, ms / steps
 
 
-def measure_ragged(steps, warmup, seed=4):
-    """64 sequences, T ~ U[1024, 8192], q in {1, 5} 1:1, E4M3 V, one launch."""
+def measure_ragged(steps, warmup, seed=4, fp8=True):
+    """64 sequences, T ~ U[1024, 8192], q in {1, 5} 1:1, E4M3 V (or bf16 V),
+    one launch per layer over 2 layer caches."""
     import torch
 
     g = torch.Generator().manual_seed(seed)
@@ -297,10 +317,10 @@ def measure_ragged(steps, warmup, seed=4):
     q_lens = [1, 5] * 32
     perm = torch.randperm(64, generator=g).tolist()
     q_lens = [q_lens[i] for i in perm]
-    cache = filled_cache(2, lens, True, seed)
+    cache = filled_cache(2, lens, fp8, seed)
     step = GraphStep(cache, q_lens, lens, seed)
     ms = time_steps(step, steps, warmup, 1)
-    byt = 2 * sum(attn_bytes(t, q, True) for t, q in zip(lens, q_lens))
+    byt = 2 * sum(attn_bytes(t, q, fp8) for t, q in zip(lens, q_lens))
     st = int(step.status.item())
     del step, cache
     torch.cuda.empty_cache()
@@ -325,6 +345,140 @@ def measure_draft(steps, warmup, seed=5):
     if st:
         raise RuntimeError(f"device status {st:#x}")
     return byt * steps / (ms * 1e-3) / 1e9, ms / steps, byt / 2
+
+
+APPEND_BYTES_PER_TOKEN = 1800  # per layer: V bf16 512 in, codes 256 + scales 8 out, K bf16 512 in + 512 out
+
+
+def measure_append(steps, warmup, n_tokens, layers=LAYERS, seed=7):
+    """BASELINE configs[2]'s append-quantize kernel (specdec_append_kv, E4M3 V): one step appends
+    `n_tokens` tokens of one sequence (2 KV heads x 128 dims) into each of `layers` layer caches
+    -- the whole 8192-token history, or one decode / verify step's 1 or 5 tokens.  Returns
+    (GB/s, us per launch); algorithmic bytes 1800 per token per layer."""
+    import torch
+
+    from specdec_b200.engine.paged_cache import PagedKVCache
+    from specdec_b200.kernels import ops
+
+    T = 8192
+    cache = PagedKVCache.allocate(layers, 1, KV, D, T, v_dtype="e4m3", device="cuda", page_order_seed=seed)
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    ks = [torch.randn(n_tokens, KV, D, generator=g, device="cuda").to(torch.bfloat16) for _ in range(layers)]
+    vs = []
+    for _ in range(layers):
+        v = torch.randn(n_tokens, KV, D, generator=g, device="cuda")
+        hit = torch.rand(v.shape, generator=g, device="cuda") < 0.01
+        sgn = torch.where(torch.rand(v.shape, generator=g, device="cuda") < 0.5, -8.0, 8.0)
+        vs.append(torch.where(hit, sgn, v).to(torch.bfloat16))
+    i32 = lambda x: torch.tensor(x, dtype=torch.int32, device="cuda")  # noqa: E731
+    row0, n_new, pos0 = i32([0]), i32([n_tokens]), i32([T - n_tokens])
+
+    class _Step:
+        def __init__(self):
+            self.graph = torch.cuda.CUDAGraph()
+
+        def run(self):
+            for layer in range(layers):
+                ops.append_kv(ks[layer], vs[layer], cache, layer, row0=row0, n_new=n_new, pos0=pos0, max_new=n_tokens)
+
+        def replay(self):
+            self.graph.replay()
+
+    st = _Step()
+    st.run()
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(st.graph, stream=s):
+            st.run()
+    torch.cuda.current_stream().wait_stream(s)
+    ms = time_steps(st, steps, warmup, 1)
+    per_launch_us = ms / steps / layers * 1e3
+    del st, cache, ks, vs
+    torch.cuda.empty_cache()
+    return n_tokens * APPEND_BYTES_PER_TOKEN / (per_launch_us * 1e-6) / 1e9, per_launch_us
+
+
+def cpu_fp8_baselines(T=8192):
+    """The reference's quantize_kv_fp8 / dequantize_kv_fp8 (model_self.py:304-320, restated bit-exactly in
+    oracle/engine.py) on the host, all threads: the V history of one layer at T tokens, and one token."""
+    import torch
+
+    from oracle.engine import dequantize_kv_fp8, quantize_kv_fp8
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(0)
+    v = torch.randn(1, KV, T, D, generator=g).to(torch.bfloat16)
+    v1 = v[:, :, :1].contiguous()
+
+    def timed(fn, budget=2.0):
+        for _ in range(3):
+            fn()
+        n, t0 = 0, time.perf_counter()
+        while True:
+            fn()
+            n += 1
+            if time.perf_counter() - t0 >= budget and n >= 20:
+                break
+        return (time.perf_counter() - t0) / n * 1e3, n
+
+    codes, scale = quantize_kv_fp8(v, 128)
+    q_ms, qn = timed(lambda: quantize_kv_fp8(v, 128))
+    d_ms, dn = timed(lambda: dequantize_kv_fp8(codes, scale, torch.bfloat16))
+    q1_ms, q1n = timed(lambda: quantize_kv_fp8(v1, 128), budget=1.0)
+    return {"quantize_kv_fp8_T8192_ms": round(q_ms, 4), "dequantize_kv_fp8_T8192_ms": round(d_ms, 4),
+            "quantize_kv_fp8_1token_ms": round(q1_ms, 4), "threads": torch.get_num_threads(), "kind": "port",
+            "sample": f"{qn}/{dn}/{q1n} calls of oracle/engine.py quantize_kv_fp8 / dequantize_kv_fp8 "
+                      f"(pinned bit-exact to the reference), V (1, 2, {T}, 128) bf16"}
+
+
+def cpu_specdec_baseline(prompt_len=128, max_new=8, k=4, seed=0):
+    """Greedy SpecDec decode tokens/s of the reference's strict executor (spec_dec.py:189-275,
+    restated in oracle/specdec.py over the oracle decoder) on the host, all threads, with the
+    configs[4] geometries (random-init bf16 Qwen2.5-1.5B target, 0.5B draft): one sequence with
+    a `prompt_len`-token uniform-random prompt -- a bounded sample of the config, whose full size
+    (256 sequences x 8192 prompt tokens) would take hours on the host."""
+    import torch
+
+    import oracle.engine as oeng
+    from oracle.specdec import spec_decode_greedy
+    from specdec_b200.engine.model import QWEN25_0P5B, QWEN25_1P5B, random_state
+
+    torch.set_num_threads(os.cpu_count() or 1)
+
+    def build(cfg, s):
+        with torch.device("meta"):
+            m = oeng.QwenLM(cfg.vocab, cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.intermediate,
+                            cfg.layers, rope_theta=cfg.rope_theta, attn_bias=cfg.attn_bias)
+        m = m.to_empty(device="cpu").to(torch.bfloat16)
+        # the GPU engine's seeded weights, drawn on the device (drawing 2 B values on the host
+        # takes minutes) and copied to host memory
+        dev = "cuda" if torch.cuda.is_available() else "cpu"
+        m.load_state_dict({k: v.cpu() for k, v in random_state(cfg, s, dev).items()}, strict=True)
+        if dev == "cuda":
+            torch.cuda.empty_cache()
+        return m.eval()
+
+    t_build = time.perf_counter()
+    tgt, drf = build(QWEN25_1P5B, seed + 1), build(QWEN25_0P5B, seed + 2)
+    t_build = time.perf_counter() - t_build
+    prompt = torch.randint(0, QWEN25_1P5B.vocab, (1, prompt_len), generator=torch.Generator().manual_seed(seed))
+    t0 = time.perf_counter()
+    with torch.inference_mode():
+        tl, _ = tgt._run(tgt.embed_tokens(prompt), None)
+        dl, _ = drf._run(drf.embed_tokens(prompt), None)
+    t_prefill = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    res = spec_decode_greedy(tgt, drf, prompt, max_new, k=k)
+    el = time.perf_counter() - t0 - t_prefill  # the executor runs its own prompt pass first
+    del tgt, drf
+    return {"decode_tokens_per_s": round(max_new / max(el, 1e-9), 3), "decode_s": round(el, 3),
+            "rounds": res["stats"]["rounds"], "accepted": res["stats"]["accepted"], "threads": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"1 sequence, prompt {prompt_len} tokens, {max_new} new tokens, k={k} (oracle/specdec.py over "
+                      f"oracle/engine.py, pinned to the reference); decode time = executor time minus one measured "
+                      f"prompt pass of both models ({t_prefill:.2f} s); weights built in {t_build:.1f} s"}
 
 
 def measure_e2e(steps, warmup, T=8192, q=5, layers=LAYERS, seed=0):
@@ -390,7 +544,7 @@ def measure_e2e(steps, warmup, T=8192, q=5, layers=LAYERS, seed=0):
     return layers * attn_bytes(T, q, False) * steps / (ms * 1e-3) / 1e9, ms / steps, h2d, d2h
 
 
-def measure_specdec(args, world, rank):
+def measure_specdec(args, world, rank, seqs=None, draft_is_target=False):
     """greedy SpecDec with random-init Qwen2.5-1.5B (target) and
     Qwen2.5-0.5B (draft) geometries, args.specdec_seqs sequences with uniform-random
     prompts of args.specdec_prompt tokens, k = 4, args.specdec_new tokens each, sharded
@@ -402,17 +556,19 @@ def measure_specdec(args, world, rank):
     from specdec_b200.engine.dp import run_specdec_dp
     from specdec_b200.engine.model import QWEN25_0P5B, QWEN25_1P5B
 
-    res = run_specdec_dp(QWEN25_1P5B, QWEN25_0P5B, total_seqs=args.specdec_seqs, prompt_len=args.specdec_prompt,
+    seqs = seqs or args.specdec_seqs
+    res = run_specdec_dp(QWEN25_1P5B, QWEN25_0P5B, total_seqs=seqs, prompt_len=args.specdec_prompt,
                          max_new=args.specdec_new, k=4, seed=0, world=world, rank=rank, target_v="e4m3",
-                         barrier=lambda: barrier(world))
-    decode_tokens = args.specdec_seqs * (args.specdec_new - 1)
+                         barrier=lambda: barrier(world), draft_is_target=draft_is_target)
+    decode_tokens = seqs * (args.specdec_new - 1)
     out = {
         "decode_tokens_per_s": round(decode_tokens / res.decode_s, 1),
         "decode_s": round(res.decode_s, 4),
         "prefill_s": round(res.prefill_s, 3),
         "rounds": res.rounds,
         "accepted_per_round": round(res.acceptance, 3),
-        "sequences": args.specdec_seqs, "prompt_len": args.specdec_prompt, "new_tokens": args.specdec_new,
+        "draft": "the target's weights (1.5B geometry)" if draft_is_target else "random-init Qwen2.5-0.5B geometry",
+        "sequences": seqs, "prompt_len": args.specdec_prompt, "new_tokens": args.specdec_new,
         "k": 4, "n_gpus": world, "parallelism": f"dp{world}", "kv": "bf16 K / E4M3 V (target), bf16 (draft)",
         "weights": "random-init bf16 (seeded, identical on every rank)",
         "tokens_checksum": int(res.tokens.long().sum()),
@@ -422,62 +578,63 @@ def measure_specdec(args, world, rank):
     return out
 
 
-def cpu_reference(calls_budget_s: float = 12.0, min_calls: int = 3, T=8192, q=5, max_calls=None):
-    """The reference's eager attention formula on the host (CPU oracle), all threads.
-
-    Returns (GB/s, calls, seconds, threads)."""
+def cpu_reference_step(layers=LAYERS, T=8192, q=5, seed=0):
+    """One step of the reference arm / CPU baseline: the verify attention of one 28-layer target
+    forward with the reference's eager formula (oracle/attention.py eager_attention, pinned to
+    reference.attention), torch CPU on all host threads, over `layers` distinct K/V histories.
+    Returns (run_step, bytes per step, threads)."""
     import torch
 
     from oracle.attention import eager_attention
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    g = torch.Generator().manual_seed(0)
-    qt = torch.randn(1, H, q, D, generator=g).to(torch.bfloat16)
-    kt = torch.randn(1, KV, T, D, generator=g).to(torch.bfloat16)
-    vt = torch.randn(1, KV, T, D, generator=g).to(torch.bfloat16)
-    for _ in range(2):
-        eager_attention(qt, kt, vt)
-    calls, t0 = 0, time.perf_counter()
-    while True:
-        eager_attention(qt, kt, vt)
-        calls += 1
-        el = time.perf_counter() - t0
-        if max_calls is not None and calls >= max_calls:
-            break
-        if calls >= min_calls and el >= calls_budget_s:
-            break
-    el = time.perf_counter() - t0
-    return attn_bytes(T, q, False) * calls / el / 1e9, calls, el, torch.get_num_threads()
+    g = torch.Generator().manual_seed(seed)
+    qs = [torch.randn(1, H, q, D, generator=g).to(torch.bfloat16) for _ in range(layers)]
+    ks = [torch.randn(1, KV, T, D, generator=g).to(torch.bfloat16) for _ in range(layers)]
+    vs = [torch.randn(1, KV, T, D, generator=g).to(torch.bfloat16) for _ in range(layers)]
+
+    def run_step():
+        for layer in range(layers):
+            eager_attention(qs[layer], ks[layer], vs[layer])
+
+    return run_step, layers * attn_bytes(T, q, False), torch.get_num_threads()
+
+
+def time_cpu_steps(run_step, steps, warmup, budget_s):
+    """Warm-up, then up to `steps` timed steps, fewer when `budget_s` would be exceeded (at
+    least 3).  Returns (seconds, steps timed, warm-up steps run)."""
+    t0 = time.perf_counter()
+    run_step()
+    per = time.perf_counter() - t0
+    warm = max(0, min(warmup, int(5.0 / max(per, 1e-9))) - 1)
+    for _ in range(warm):
+        run_step()
+    timed = max(3, min(steps, int(budget_s / max(per, 1e-9))))
+    t0 = time.perf_counter()
+    for _ in range(timed):
+        run_step()
+    return time.perf_counter() - t0, timed, warm + 1
 
 
 # ------------------------------------------------------------------------------ arms
 def run_reference_arm(args, world, rank):
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
-    per_call = None
-    # one step = one verify-attention call of the reference's eager formula; bounded so the whole
-    # run stays within about a minute whatever --steps is
-    gbs, calls, el, thr = cpu_reference(calls_budget_s=0.0, min_calls=1, max_calls=1)
-    per_call = el / calls
-    total_budget = 60.0
-    warm = min(args.warmup, max(1, int(5.0 / per_call)))
-    timed = min(args.steps, max(3, int(total_budget / per_call)))
-    for _ in range(warm):
-        cpu_reference(0.0, 1, max_calls=1)
-    gbs, calls, el, thr = cpu_reference(calls_budget_s=1e9, min_calls=timed, max_calls=timed)
+    run_step, byt, thr = cpu_reference_step()
+    el, timed, warm = time_cpu_steps(run_step, args.steps, args.warmup, 60.0)
+    gbs = byt * timed / el / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
-        "steps": calls, "warmup": warm, "ms_per_step": round(el / calls * 1e3, 3), "higher_is_better": True,
+        "steps": timed, "warmup": warm, "ms_per_step": round(el / timed * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "verify-attn q5 T8192 batch1, one layer call per step (configs[1])",
-                   "model": "Qwen2.5-1.5B attention geometry 12:2 d128", "global_batch": 1, "seq_len": 8192,
-                   "parallelism": "host cores"},
+        "config": {"workload": "verify-attn q5 T8192 batch1 per GPU x 28 layer caches per step (configs[1])",
+                   "model": "Qwen2.5-1.5B attention geometry 12:2 d128, bf16 K/V", "global_batch": 1,
+                   "seq_len": 8192, "parallelism": "host cores"},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": thr, "kind": "port",
-                         "sample": f"{calls} calls of the reference eager attention formula "
-                                   f"(oracle/attention.py eager_attention, torch CPU, {thr} threads); "
-                                   f"steps capped to ~{int(total_budget)} s"},
+                         "sample": f"{timed} steps x 28 layer calls of the reference eager attention formula "
+                                   f"(oracle/attention.py eager_attention, pinned to reference.attention; torch CPU, "
+                                   f"{thr} threads); steps capped to ~60 s"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -494,21 +651,26 @@ def run_ours(args, world, rank, local):
     cache = filled_cache(LAYERS, [T], False, seed=rank)
     step = GraphStep(cache, [q], [T], seed=rank)
     with ClockSampler(local) as clk:
-        ms = time_steps(step, args.steps, args.warmup, world)
+        windows = time_windows(step, args.steps, args.warmup, world)
     st = int(step.status.item())
     if st:
         raise RuntimeError(f"device status {st:#x}: {_lib.status_message(st)}")
-    ms_max = max_over_ranks(ms, world)
+    ms_max = statistics.median(windows)
     per_call = attn_bytes(T, q, False)
     value = world * LAYERS * per_call * args.steps / (ms_max * 1e-3) / 1e9
     launches = step.launches_per_step * args.steps
     del step
-    # the dominant kernel's own duration: a second graph of the same step with CUDA
-    # events around every attention kernel (event nodes add gaps, so this graph is
-    # not the one the value above comes from)
+    # the dominant kernel's in-step duration: the same step's 28 verify launches without the
+    # plan, replayed as one graph (programmatic dependent launches, as in the step), timed with
+    # CUDA events over the replays -- 28 x launch_ms never exceeds ms_per_step
+    vstep = GraphStep(cache, [q], [T], seed=rank, with_plan=False)
+    v_ms = statistics.median(time_windows(vstep, max(args.steps, 50), args.warmup, world))
+    launch_ms = v_ms / max(args.steps, 50) / LAYERS
+    del vstep
+    # the same kernels with CUDA events right around every launch (no overlap with neighbours)
     ev_step = GraphStep(cache, [q], [T], seed=rank, events=True)
     time_steps(ev_step, max(20, min(args.steps, 200)), args.warmup, world)
-    split_ms = ev_step.split_ms()
+    isolated_ms = ev_step.split_ms()
     del ev_step, cache
     torch.cuda.empty_cache()
 
@@ -521,17 +683,31 @@ def run_ours(args, world, rank, local):
             for qq in (1, 5):
                 gbs, mss = measure_config(TT, qq, False, ks, 5)
                 extras[f"bf16_T{TT}_q{qq}"] = {"GB/s": round(gbs, 1), "pct_of_8TBs": round(gbs / 80.0, 2),
-                                              "ms_per_step": round(mss, 4)}
+                                              "frac_of_measured_peak": round(gbs / peak, 4),
+                                              "us_per_layer": round(mss / LAYERS * 1e3, 3)}
         for qq in (1, 5):
             gbs, mss = measure_config(8192, qq, True, ks, 5)
             extras[f"e4m3v_T8192_q{qq}"] = {"GB/s": round(gbs, 1), "pct_of_8TBs": round(gbs / 80.0, 2),
-                                           "ms_per_step": round(mss, 4)}
-        gbs, mss, byt = measure_ragged(max(20, min(args.steps, 200)), 5)
-        extras["ragged64_e4m3v"] = {"GB/s": round(gbs, 1), "pct_of_8TBs": round(gbs / 80.0, 2),
-                                    "ms_per_layer": round(mss / 2, 4), "bytes_per_layer": int(byt)}
+                                           "frac_of_measured_peak": round(gbs / peak, 4),
+                                           "us_per_layer": round(mss / LAYERS * 1e3, 3)}
+        for fp8 in (True, False):
+            gbs, mss, byt = measure_ragged(max(20, min(args.steps, 200)), 5, fp8=fp8)
+            extras["ragged64_e4m3v" if fp8 else "ragged64_bf16"] = {
+                "GB/s": round(gbs, 1), "pct_of_8TBs": round(gbs / 80.0, 2), "frac_of_measured_peak": round(gbs / peak, 4),
+                "us_per_layer": round(mss / 2 * 1e3, 2), "bytes_per_layer": int(byt)}
         gbs, mss, byt = measure_draft(max(20, min(args.steps, 200)), 5)
         extras["draft64_d64_q1_T8192"] = {"GB/s": round(gbs, 1), "pct_of_8TBs": round(gbs / 80.0, 2),
-                                          "ms_per_layer": round(mss / 2, 4), "bytes_per_layer": int(byt)}
+                                          "frac_of_measured_peak": round(gbs / peak, 4),
+                                          "us_per_layer": round(mss / 2 * 1e3, 2), "bytes_per_layer": int(byt)}
+        app = {}
+        for n_tok, label in ((8192, "history_T8192"), (1, "decode_1token"), (5, "verify_5tokens")):
+            gbs, us = measure_append(max(20, min(args.steps, 200)), 5, n_tok)
+            app[label] = {"GB/s": round(gbs, 1), "frac_of_measured_peak": round(gbs / peak, 4),
+                          "us_per_launch": round(us, 3), "bytes_per_launch": n_tok * APPEND_BYTES_PER_TOKEN}
+        app["note"] = ("specdec_append_kv with E4M3 V, one sequence x 2 KV heads x 128 dims, 28 layer caches per "
+                       "step; algorithmic bytes 1800 per token per layer (V 512 in, codes 256 + scales 8 out, "
+                       "K 512 in + 512 out)")
+        extras["append_quantize_configs2"] = app
     if not args.no_extras:
         e_gbs, e_ms, h2d, d2h = measure_e2e(max(5, min(args.steps, 100)), 3)
         e2e = {"value": round(e_gbs * world, 3), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
@@ -541,16 +717,26 @@ def run_ours(args, world, rank, local):
                        "CUDA graph and replayed"}
         e_ms_max = max_over_ranks(e_ms, world)
         e2e["value"] = round(world * LAYERS * per_call / (e_ms_max * 1e-3) / 1e9, 3)
-    specdec = None
+    specdec = specdec_full = None
     if not args.no_specdec:
         specdec = measure_specdec(args, world, rank)
+        if not args.no_extras:
+            specdec_full = measure_specdec(args, world, rank, seqs=max(world, args.specdec_seqs // 4),
+                                           draft_is_target=True)
+    cpu_extra = None
     if rank == 0 and not args.no_extras:
-        c_gbs, calls, el, thr = cpu_reference()
+        run_step, byt, thr = cpu_reference_step()
+        el, timed, _ = time_cpu_steps(run_step, 1000, 3, 15.0)
+        c_gbs = byt * timed / el / 1e9
         cpu = {"value": round(c_gbs, 3), "unit": "GB/s", "cores": thr, "kind": "port",
-               "sample": f"{calls} calls ({el:.1f} s) of the reference eager attention formula at q5 T8192 "
-                         f"(oracle/attention.py, torch CPU, {thr} threads)"}
+               "sample": f"{timed} steps x 28 layer calls ({el:.1f} s) of the reference eager attention formula at "
+                         f"q5 T8192 (oracle/attention.py, pinned to reference.attention; torch CPU, {thr} threads)"}
+        del run_step
+        cpu_extra = {"fp8_quantiser": cpu_fp8_baselines()}
+        if not args.no_specdec:
+            cpu_extra["spec_decode_greedy"] = cpu_specdec_baseline()
 
-    achieved = per_call / (split_ms * 1e-3) / 1e9
+    achieved = per_call / (launch_ms * 1e-3) / 1e9
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -561,6 +747,7 @@ def run_ours(args, world, rank, local):
                                 "random page order",
                        "global_batch": world, "seq_len": T, "parallelism": f"dp{world}",
                        "l2": "inputs larger than L2: 28 distinct layer caches = 235 MB read per step"},
+            "windows_ms": [round(w, 4) for w in windows],
             "pct_of_8TBs_per_gpu": round(value / world / 80.0, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": NCU_TRAFFIC_VERIFY8K,
@@ -568,13 +755,18 @@ def run_ours(args, world, rank, local):
                                            "bench.py --profile-case verify8k",
                          "kernel": "verify_kernel<32,bf16V,pool> (tcgen05)", "peak_kind": peak_kind,
                          "algorithmic_bytes_per_launch": per_call,
-                         "launch_ms": round(split_ms, 5)},
+                         "launch_ms": round(launch_ms, 5),
+                         "launch_ms_source": "in-step: graph of the step's 28 verify launches (no plan), CUDA events "
+                                             "over its replays / 28",
+                         "launch_ms_isolated": round(isolated_ms, 5)},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches,
             "clocks": clk.summary(),
             "extras": extras,
+            "cpu_extras": cpu_extra,
             "specdec_e2e": specdec,
+            "specdec_e2e_full_accept": specdec_full,
         }
         print(json.dumps(line), flush=True)
 

@@ -11,6 +11,8 @@ replaces (RichardF123/SpecDec-Context-Scaling):
   accept.py     greedy accept, strict and vectorised     (spec_dec.py:230-250,
                                                           fast_spec_dec.py:246-256)
   engine.py     a small Qwen2 decoder with the reference cache semantics (model_self.py:668-931)
+  elementwise.py reference.rmsnorm / apply_rope / swiglu  (specdec/kernels/reference.py:14-31)
+  specdec.py    the strict greedy SpecDec executor       (specdec/engine/spec_dec.py:189-275)
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import
 it, always as the checker or the timed CPU baseline; the product path

@@ -78,9 +78,11 @@ class DPResult:
 
 def run_specdec_dp(target_cfg, draft_cfg, *, total_seqs: int, prompt_len: int, max_new: int, k: int = 4,
                    seed: int = 0, world: int = 1, rank: int = 0, target_v: str = "bf16", chunk: int = 4,
-                   barrier=None) -> DPResult:
+                   barrier=None, draft_is_target: bool = False) -> DPResult:
     """One data-parallel SpecDec job on this rank's GPU (weights from ``seed``).  The
-    decode time is the device time of the round-graph replays (CUDA events)."""
+    decode time is the device time of the round-graph replays (CUDA events).
+    ``draft_is_target``: the draft runs the target's weights (``draft_cfg`` is ignored), so
+    nearly every candidate is accepted -- the full-accept path of every round."""
     from .model import PagedModel
     from .specdec import SpecDecEngine
 
@@ -88,8 +90,15 @@ def run_specdec_dp(target_cfg, draft_cfg, *, total_seqs: int, prompt_len: int, m
     dev = torch.device("cuda", torch.cuda.current_device())
     s, e = shard_bounds(total_seqs, world, rank)
     prompts = synthetic_prompts(total_seqs, prompt_len, target_cfg.vocab, seed)[s:e].to(dev)
-    target = PagedModel.random(target_cfg, seed + 1, dev)
-    draft = PagedModel.random(draft_cfg, seed + 2, dev)
+    if draft_is_target:
+        from .model import random_state
+
+        state = random_state(target_cfg, seed + 1, dev)
+        target, draft = PagedModel(target_cfg, state, dev), PagedModel(target_cfg, state, dev)
+        del state
+    else:
+        target = PagedModel.random(target_cfg, seed + 1, dev)
+        draft = PagedModel.random(draft_cfg, seed + 2, dev)
     eng = SpecDecEngine(target, draft, e - s, prompt_len, max_new, k=k, target_v=target_v)
     eng.capture()  # warm-up round + graph capture on the empty state; prefill resets it
     sync = barrier or (lambda: None)

@@ -209,3 +209,49 @@ def test_specdec_mixed_acceptance_freezes_finished_sequences():
     # freezing it would have grown past the caches' capacity
     assert int(acc.max() - acc.min()) >= 2 * (k + 1), acc.tolist()
     assert int(eng.tc.lengths.max()) <= P + N + 2 * (k + 1)
+
+
+@pytest.mark.parametrize("fmt", ["fp16", "v_fp8"])
+def test_paged_engine_matches_reference_golden(golden, fmt):
+    """The paged decoder and the SpecDec engine against the reference model's own outputs
+    (a tiny random-init reference QwenLM, model_self.py:835-931, run on the CPU by
+    tests/golden/make_golden.py): prompt-pass logits, the logits of a 5-token verify block
+    on the prompt's cache, and greedy tokens (SpecDec with the target as its own draft),
+    for the bf16 and V-only FP8 cache formats.  Greedy tokens may differ only at a
+    documented near-tie of the reference's logits."""
+    from specdec_b200.engine.model import ModelConfig, PagedModel, StepLayout
+    from specdec_b200.engine.specdec import SpecDecEngine
+    from specdec_b200.kernels import ops
+
+    g = golden["model"]
+    c = g["config"]
+    cfg = ModelConfig(vocab=c["vocab"], hidden=c["hidden"], heads=c["heads"], kv_heads=c["kv_heads"],
+                      head_dim=c["head_dim"], intermediate=c["intermediate"], layers=c["layers"],
+                      rope_theta=c["rope_theta"], eps=c["eps"], attn_bias=c["attn_bias"])
+    state = {k: v.cuda() for k, v in g["state"].items()}
+    pm = PagedModel(cfg, state)
+    want = g[fmt]
+    v_dtype = "e4m3" if fmt == "v_fp8" else "bf16"
+    prompt = g["prompt"].to(torch.int32).cuda()
+    P = prompt.shape[1]
+    cache = pm.new_cache(1, 64, v_dtype)
+    with torch.inference_mode():
+        lg = pm.prefill(prompt, cache, 0)
+        _close(lg[0].cpu(), want["prompt_logits"], f"{fmt} prompt logits")
+        lay = StepLayout(1, 5, "cuda")
+        ws = ops.attn_workspace(lay.batch, cfg.heads, cache)
+        lay.set(cache.lengths)
+        h = pm.step(g["block"].to(torch.int32).cuda().reshape(-1), lay, cache, ws)
+        _close(pm.logits(h).cpu(), want["verify_logits"], f"{fmt} verify-block logits")
+    N = len(want["greedy"])
+    eng = SpecDecEngine(pm, PagedModel(cfg, state), 1, P, N, k=4, target_v=v_dtype, draft_v=v_dtype)
+    eng.capture()
+    eng.prefill(prompt)
+    eng.decode()
+    got = eng.tokens()[0].cpu().tolist()
+    lgs = want["greedy_logits"].float()
+    for i, (a, b) in enumerate(zip(got, want["greedy"])):
+        if a != b:
+            top = torch.topk(lgs[i], 2).values
+            assert float(top[0] - top[1]) < NEAR_TIE, f"{fmt}: token {i} differs ({a} vs {b}) with no near-tie"
+            break

@@ -190,3 +190,27 @@ def test_engine_oracle_matches_reference_model(golden, fmt):
         assert torch.equal(vb[0], want["verify_logits"])
         toks, _ = oeng.greedy_decode(m, g["prompt"], len(want["greedy"]))
     assert toks == want["greedy"]
+
+
+def test_specdec_oracle_replays_reference_executor_traces(golden):
+    """oracle/specdec.py (the strict executor restated, spec_dec.py:189-275) on the toy models
+    the golden traces were recorded with: the same emitted tokens and, round by round, the
+    same candidates, argmaxes, accepted counts, emitted tokens and cache lengths."""
+    import importlib.util
+    from pathlib import Path
+
+    from oracle import specdec as osd
+
+    spec = importlib.util.spec_from_file_location("make_golden", Path(__file__).parent / "golden" / "make_golden.py")
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    for tr in golden["traces"]:
+        tgt = mg.ToyLM(tr["vocab"], tr["hidden"], tr["seed"])
+        drf = mg.ToyLM(tr["vocab"], tr["hidden"], tr["seed"] + 50, like=tgt, noise=tr["noise"])
+        log = []
+        res = osd.spec_decode_greedy(tgt, drf, tr["prompt"], tr["max_new"], k=4, log=log.append)
+        assert res["gen"] == tr["gen"]
+        assert len(log) == len(tr["control"])
+        for mine, ref in zip(log, tr["control"]):
+            for key in ("Kp", "m", "pre", "tgt_len", "drf_len", "cands", "g", "emitted"):
+                assert mine[key] == ref[key], (tr["seed"], key)
