@@ -139,9 +139,11 @@ __global__ void __launch_bounds__(256) rope_kernel(const T* __restrict__ x, int6
   const int half = D / 2;
   const float xv = to_f<T>(xr[d]);
   const float rot = d < half ? -to_f<T>(xr[d + half]) : to_f<T>(xr[d - half]);
-  const float a = round_to<T>(xv * to_f<T>(cs[s * D + d]));
-  const float c = round_to<T>(rot * to_f<T>(sn[s * D + d]));
-  y[idx] = from_f<T>(a + c);
+  // one rounding per torch op (x * cos, rotate_half(x) * sin, their sum): explicit IEEE
+  // products and sum, so no fused multiply-add merges them for fp32
+  const float a = round_to<T>(__fmul_rn(xv, to_f<T>(cs[s * D + d])));
+  const float c = round_to<T>(__fmul_rn(rot, to_f<T>(sn[s * D + d])));
+  y[idx] = from_f<T>(__fadd_rn(a, c));
 }
 
 template <typename T>

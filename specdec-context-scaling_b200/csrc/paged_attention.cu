@@ -47,9 +47,9 @@ static_assert(sizeof(WorkItem) == 48, "work item is 48 bytes");
 // item and that item's first 32 page ids (0 past the item), and for after its items the
 // merge counts -- one 256-byte line.
 struct CtaDesc {
-  WorkItem first;
+  WorkItem first;  // cluster mode: the CTA's group (its item, or the group's fields when it has no pages)
   int32_t item_begin, item_end;  // the CTA's items: [item_begin, item_end) (every CTA of the grid)
-  int32_t pad0[2];
+  int32_t cl_first, cl_count;    // cluster mode: the group's first cluster and cluster count (0: idle)
   int32_t pages[32];
   // the plan header's merge counts and CTA count, so the merge needs no header load
   int32_t num_merge_wide, num_merge_narrow, num_ctas;
@@ -79,7 +79,7 @@ constexpr int kStatStride = 8;
 constexpr int kMergeWide = 16;  // groups with at least this many splits are merged by whole CTAs
 
 struct WsLayout {
-  size_t items, groups, ctas, cdesc, mlist, lse, po, total;
+  size_t items, groups, ctas, cdesc, mlist, tickets, lse, po, total;
   int32_t max_items, max_groups;
 };
 
@@ -92,7 +92,8 @@ static WsLayout ws_layout(int B, int KV, int max_qtiles, int D, int target_items
   w.ctas = align_up(w.groups + sizeof(GroupInfo) * (size_t)w.max_groups, 256);
   w.cdesc = align_up(w.ctas + sizeof(int32_t) * (size_t)(target_items / 4 + 1), 256);
   w.mlist = align_up(w.cdesc + sizeof(CtaDesc) * (size_t)(target_items / 4 + 1), 256);
-  w.lse = align_up(w.mlist + sizeof(GroupInfo) * (size_t)w.max_groups, 256);
+  w.tickets = align_up(w.mlist + sizeof(GroupInfo) * (size_t)w.max_groups, 256);
+  w.lse = align_up(w.tickets + sizeof(int32_t) * kMaxRows * (size_t)(target_items / 4 + 1), 256);
   w.po = align_up(w.lse + sizeof(float) * kStatStride * kMaxRows * (size_t)w.max_items, 256);
   w.total = align_up(w.po + sizeof(float) * kMaxRows * (size_t)D * w.max_items, 256);
   return w;
@@ -125,6 +126,11 @@ struct AttnParams {
   int32_t tile_pages;  // the verify kernel consumes keys in tiles of this many pages
   int32_t early_loads;  // 1: plan, page table and KV history may be read before the dependency wait
   int32_t* status;
+  // cluster mode (cluster_size > 0): the grid is num_clusters clusters of cluster_size CTAs;
+  // every cluster works on one group and reduces its CTAs' partials in distributed shared
+  // memory; groups spread over several clusters meet through per-row tickets
+  int32_t cluster_size, num_clusters;
+  int32_t* tickets;  // [num_clusters][kMaxRows]: arrivals of a group's clusters per row
 };
 
 SD_DEV int seq_q_len(const AttnParams& p, int b) { return p.q_len ? p.q_len[b] : p.uni_q_len; }
@@ -186,7 +192,113 @@ SD_DEV int block_exclusive_scan(int v, int& total, int* s_warp) {
   return before + x - v;
 }
 
+// ---------------------------------------------------------------- cluster-mode plan
+// Small batches (every group fits a cluster of its own) run the verify kernel as
+// num_clusters clusters of cluster_size CTAs.  Group g gets c_g clusters: the fewest tiles
+// per CTA k such that sum_g ceil(tiles_g / (cluster_size k)) clusters fit the grid, with
+// c_g = ceil(tiles_g / (cluster_size k)); its c_g * cluster_size CTAs split the group's
+// 128-key tiles evenly (some CTAs of a short group get none).  Clusters without a group
+// come first in the grid (dispatched first, they leave at once).  One item per CTA, item
+// index = block index.  The per-row tickets of the clusters start at zero.
+constexpr int kClusterMaxGroups = 32;
+SD_DEV void cluster_plan(const AttnParams& p) {
+  __shared__ int s_pages[kClusterMaxGroups], s_c[kClusterMaxGroups], s_cl0[kClusterMaxGroups];
+  const int G = p.max_groups, CS = p.cluster_size, NC = p.num_clusters, grid = NC * CS;
+  const int t = threadIdx.x;
+  if (t < kClusterMaxGroups) {
+    int b, h, q0, nq;
+    s_pages[t] = t < G ? group_pages(p, t, b, h, q0, nq) : 0;
+  }
+  __syncthreads();
+  if (t == 0) {
+    int k = 1;
+    for (;; ++k) {
+      int need = 0;
+      for (int g = 0; g < G; ++g) {
+        const int tiles = (s_pages[g] + kPlanTilePages - 1) / kPlanTilePages;
+        need += (tiles + CS * k - 1) / (CS * k);
+      }
+      if (need <= NC) break;
+    }
+    int used = 0;
+    for (int g = 0; g < G; ++g) {
+      const int tiles = (s_pages[g] + kPlanTilePages - 1) / kPlanTilePages;
+      s_c[g] = (tiles + CS * k - 1) / (CS * k);
+      used += s_c[g];
+    }
+    int cl = NC - used;  // idle clusters first
+    for (int g = 0; g < G; ++g) {
+      s_cl0[g] = cl;
+      cl += s_c[g];
+    }
+  }
+  __syncthreads();
+  for (int x = t; x < grid; x += blockDim.x) {
+    const int cl = x / CS, cr = x - cl * CS;
+    int g = -1;
+    for (int j = 0; j < G; ++j)
+      if (s_c[j] > 0 && cl >= s_cl0[j] && cl < s_cl0[j] + s_c[j]) g = j;
+    CtaDesc& d = p.cdesc[x];
+    WorkItem it;
+    memset(&it, 0, sizeof(it));
+    d.cl_first = 0;
+    d.cl_count = 0;
+    if (g >= 0) {
+      int b, h, q0, nq;
+      const int P = group_pages(p, g, b, h, q0, nq);
+      const int n = s_c[g] * CS, j = (cl - s_cl0[g]) * CS + cr;
+      const int tiles = (P + kPlanTilePages - 1) / kPlanTilePages;
+      const int t0 = static_cast<int>(static_cast<long long>(j) * tiles / n);
+      const int t1 = static_cast<int>(static_cast<long long>(j + 1) * tiles / n);
+      it.b = b;
+      it.h = h;
+      it.q0 = q0;
+      it.nq = nq;
+      it.page_begin = min(t0 * kPlanTilePages, P);
+      it.page_end = min(t1 * kPlanTilePages, P);
+      it.group = g;
+      it.nsplit = n;  // > 1: the epilogue writes a partial
+      it.ctx = seq_ctx_len(p, b);
+      it.qlen = seq_q_len(p, b);
+      it.row0 = seq_row0(p, b);
+      it.cta = x;
+      d.cl_first = s_cl0[g];
+      d.cl_count = s_c[g];
+    }
+    p.items[x] = it;
+    d.first = it;
+    d.item_begin = x;
+    d.item_end = x + (it.page_end > it.page_begin ? 1 : 0);
+    d.num_merge_wide = 0;
+    d.num_merge_narrow = 0;
+    d.num_ctas = grid;
+  }
+  __syncthreads();
+  for (int u = t; u < grid * 32; u += blockDim.x) {
+    const int x = u >> 5, kk = u & 31;
+    const WorkItem& it = p.cdesc[x].first;
+    p.cdesc[x].pages[kk] = (p.page_table != nullptr && kk < it.page_end - it.page_begin)
+                               ? p.page_table[static_cast<int64_t>(it.b) * p.max_pages + it.page_begin + kk]
+                               : 0;
+  }
+  for (int i = t; i < NC * kMaxRows; i += blockDim.x) p.tickets[i] = 0;
+  if (t == 0) {
+    p.hdr->num_items = grid;
+    p.hdr->pages_per_split = 0;
+    p.hdr->num_groups = G;
+    p.hdr->bar_arrive = 0ull;
+    p.hdr->num_merge_wide = 0;
+    p.hdr->num_merge_narrow = 0;
+    p.hdr->total_pages = 0;
+    p.hdr->num_ctas = grid;
+  }
+}
+
 __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
+  if (p.cluster_size > 0) {
+    cluster_plan(p);
+    return;
+  }
   __shared__ int s_warp[32];
   __shared__ long long s_total;
   __shared__ int s_rows;
@@ -558,6 +670,140 @@ SD_DEV bool grid_barrier(unsigned long long* counter, unsigned n_ctas, bool wait
     __nanosleep(64);
   }
   return true;
+}
+
+// ---------------------------------------------------------------- cluster-mode merge
+// After its item every CTA of a cluster holds, in its own shared memory, the split partial
+// of its key range: per query row the unnormalised O row (D floats at cl_o + row * D) and
+// the statistics (row max, four key-quarter sums at cl_st + row * kStatStride); a CTA
+// without pages holds zero rows with max -inf.  After a cluster barrier, CTA rank cr owns
+// rows cr, cr + CS, ... and combines the CS partials of each through distributed shared
+// memory (warps take the (row, peer) units in turn; states combined max-first in this CTA's
+// scratch `s_st`, which no peer reads).  A group on one cluster writes the output row; a
+// group on c > 1 clusters writes the cluster's partial of the row to the workspace
+// (slot = cluster index), and the row's last-arriving cluster (per-row ticket, counted
+// after a release fence) combines the c partials, writes the output and resets the ticket.
+constexpr int kClusterMaxOwn = 4;  // rows per CTA: at most 32 rows over clusters of >= 8 CTAs
+
+template <int D, int NWARP>
+SD_DEV void cluster_merge(const AttnParams& p, const CtaDesc& cd, const float* cl_o, const float* cl_st,
+                          MergeState* s_st, int warp, int lane) {
+  constexpr int NQ = D / 4;     // dim quads: lanes per row
+  constexpr int SPW = 32 / NQ;  // units per warp step
+  const int quad = lane % NQ, slot = lane / NQ;
+  const int CS = static_cast<int>(cluster_nctarank()), cr = static_cast<int>(cluster_ctarank());
+  const WorkItem& g = cd.first;
+  const int R = p.n_rep * g.nq;
+  const int own = R > cr ? (R - cr + CS - 1) / CS : 0;  // rows cr, cr + CS, ...
+  const uint32_t o_base = smem_u32(cl_o), st_base = smem_u32(cl_st);
+
+  MergeState st[kClusterMaxOwn];
+#pragma unroll
+  for (int j = 0; j < kClusterMaxOwn; ++j) {
+    st[j].m = -INFINITY;
+    st[j].l = 0.f;
+    st[j].a = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const int units = own * CS;
+  for (int u0 = warp * SPW; u0 < units; u0 += NWARP * SPW) {
+    const int u = u0 + slot;
+    if (u < units) {
+      const int j = u / CS, peer = u - j * CS;
+      const int row = cr + j * CS;
+      const float4 s4 = dsmem_ld4(dsmem_addr(st_base + row * kStatStride * 4, peer));
+      const float l3 = dsmem_ld(dsmem_addr(st_base + (row * kStatStride + 4) * 4, peer));
+      MergeState o;
+      o.m = s4.x;
+      o.l = (s4.y + s4.z) + (s4.w + l3);
+      o.a = dsmem_ld4(dsmem_addr(o_base + (row * D + 4 * quad) * 4, peer));
+#pragma unroll
+      for (int jj = 0; jj < kClusterMaxOwn; ++jj)
+        if (jj == j) merge_combine(st[jj], o);
+    }
+  }
+  // the warp's two unit slots (head_dim 64) hold different units of possibly the same row:
+  // fold slot 1 into slot 0 row by row, then publish the warp's states
+#pragma unroll
+  for (int j = 0; j < kClusterMaxOwn; ++j) {
+    if (SPW == 2) {
+      MergeState o;
+      o.m = __shfl_xor_sync(0xffffffffu, st[j].m, 16);
+      o.l = __shfl_xor_sync(0xffffffffu, st[j].l, 16);
+      o.a.x = __shfl_xor_sync(0xffffffffu, st[j].a.x, 16);
+      o.a.y = __shfl_xor_sync(0xffffffffu, st[j].a.y, 16);
+      o.a.z = __shfl_xor_sync(0xffffffffu, st[j].a.z, 16);
+      o.a.w = __shfl_xor_sync(0xffffffffu, st[j].a.w, 16);
+      merge_combine(st[j], o);
+    }
+    if (j < own) s_st[(j * NWARP + warp) * 32 + lane] = st[j];
+  }
+  __syncthreads();
+  if (warp >= own || slot != 0) return;
+  // warp j finishes row cr + j * CS: the warps' states, common max first
+  const int j = warp, row = cr + j * CS;
+  MergeState tot;
+  {
+    float m = -INFINITY;
+#pragma unroll 1
+    for (int w = 0; w < NWARP; ++w) m = fmaxf(m, s_st[(j * NWARP + w) * 32 + lane].m);
+    tot.m = m;
+    tot.l = 0.f;
+    tot.a = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (m != -INFINITY) {
+#pragma unroll 1
+      for (int w = 0; w < NWARP; ++w) {
+        const MergeState o = s_st[(j * NWARP + w) * 32 + lane];
+        const float wt = fast_exp2(o.m - m);
+        tot.a.x += o.a.x * wt;
+        tot.a.y += o.a.y * wt;
+        tot.a.z += o.a.z * wt;
+        tot.a.w += o.a.w * wt;
+        tot.l += o.l * wt;
+      }
+    }
+  }
+  const unsigned lanes = NQ == 32 ? 0xffffffffu : 0x0000ffffu;
+  if (cd.cl_count > 1) {
+    // this cluster's partial of the row, then the row's ticket
+    const int cl = static_cast<int>(cluster_id_x());
+    const int64_t slot_row = static_cast<int64_t>(cl) * kMaxRows + row;
+    reinterpret_cast<float4*>(p.p_o + slot_row * D)[quad] = tot.a;
+    if (quad == 0) {
+      p.p_stat[slot_row * kStatStride] = tot.m;
+      p.p_stat[slot_row * kStatStride + 1] = tot.l;
+    }
+    __threadfence();
+    __syncwarp(lanes);
+    int last = 0;
+    if (quad == 0) {
+      const int old = atomicAdd(&p.tickets[static_cast<int64_t>(cd.cl_first) * kMaxRows + row], 1);
+      last = old == cd.cl_count - 1;
+    }
+    last = __shfl_sync(lanes, last, 0);
+    if (!last) return;
+    __threadfence();
+    tot.m = -INFINITY;
+    tot.l = 0.f;
+    tot.a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+    for (int c = 0; c < cd.cl_count; ++c) {
+      const int64_t sr = static_cast<int64_t>(cd.cl_first + c) * kMaxRows + row;
+      MergeState o;
+      o.m = __ldcg(p.p_stat + sr * kStatStride);
+      o.l = __ldcg(p.p_stat + sr * kStatStride + 1);
+      o.a = __ldcg(reinterpret_cast<const float4*>(p.p_o + sr * D) + quad);
+      merge_combine(tot, o);
+    }
+    if (quad == 0) p.tickets[static_cast<int64_t>(cd.cl_first) * kMaxRows + row] = 0;
+  }
+  const float inv = tot.l > 0.f ? 1.f / tot.l : 0.f;
+  const int hh = row / g.nq, qi = g.q0 + row % g.nq;
+  __nv_bfloat16* dst = p.out + static_cast<int64_t>(g.row0 + qi) * p.o_st +
+                       static_cast<int64_t>(g.h * p.n_rep + hh) * p.o_sh + quad * 4;
+  uint2 pk;
+  pk.x = pack_bf16(tot.a.x * inv, tot.a.y * inv);
+  pk.y = pack_bf16(tot.a.z * inv, tot.a.w * inv);
+  *reinterpret_cast<uint2*>(dst) = pk;
 }
 
 #include "verify_kernel.cuh"

@@ -81,6 +81,16 @@ def random_state(cfg: ModelConfig, seed: int, device="cuda", std: float = 0.02, 
     return sd
 
 
+def _e4m3_round_trip(v: torch.Tensor) -> torch.Tensor:
+    """bf16(e4m3(v / s) * s) with s = max|v| / 448 per token row (1 for an all-zero row): the
+    values specdec_append_kv's codes and scales stand for (quantize_kv_fp8 with one group per
+    head, model_self.py:304-320).  Used by the prompt pass only."""
+    x = v.float()
+    s = x.abs().amax(dim=-1, keepdim=True) / 448.0
+    s = torch.where(s == 0, torch.ones_like(s), s)
+    return ((x / s).to(torch.float8_e4m3fn).float() * s).to(v.dtype)
+
+
 @dataclass
 class _Layer:
     w_qkv: torch.Tensor
@@ -247,6 +257,11 @@ class PagedModel:
             q, k, v = self._qkv(L, h, cos, sin)
             ops.append_kv(k[0].transpose(0, 1), v.transpose(0, 1), cache, li, row0=row0, n_new=n_new, pos0=pos0,
                           max_new=P, status=status)
+            if cache.v_dtype == "e4m3":
+                # the prompt attends over the V the pool now holds (E4M3 codes times their
+                # scales), as the reference's V-only FP8 prompt pass attends over
+                # dequantize(quantize(v)) (model_self.py:702-704)
+                v = _e4m3_round_trip(v)
             q4 = q[0].view(c.heads, n, P, c.head_dim).transpose(0, 1)
             k4 = k[0].view(c.kv_heads, n, P, c.head_dim).transpose(0, 1).repeat_interleave(n_rep, dim=1)
             v4 = v.view(c.kv_heads, n, P, c.head_dim).transpose(0, 1).repeat_interleave(n_rep, dim=1)

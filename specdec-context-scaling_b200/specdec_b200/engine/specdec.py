@@ -73,6 +73,7 @@ class SpecDecEngine:
         self.new_tlen = torch.zeros(num_seqs, **i32)
         self.new_dlen = torch.zeros(num_seqs, **i32)
         self.accepted = torch.zeros(num_seqs, dtype=torch.int64, device=dev)
+        self.active_rounds = torch.zeros(num_seqs, dtype=torch.int64, device=dev)
         self.rounds = 0
         self.status = torch.zeros(1, **i32)
         self.acc_ws = ops.accept_workspace(num_seqs, k + 1, target.cfg.vocab, dev)
@@ -99,6 +100,7 @@ class SpecDecEngine:
         self.active.fill_(1)
         self.catch.zero_()
         self.accepted.zero_()
+        self.active_rounds.zero_()
         self.rounds = 0
 
     # ------------------------------------------------------------------ one round
@@ -139,6 +141,7 @@ class SpecDecEngine:
         self.out.scatter_(1, pos, torch.where(keep, vals, self.out.gather(1, pos)))
         self.n_out.add_((self.m + 1) * act)
         self.accepted.add_(self.m)  # 0 for frozen sequences
+        self.active_rounds.add_(act)
         # 4. rollback on the device (accept keeps a frozen sequence's target length)
         self.tc.lengths.copy_(self.new_tlen)
         full = (self.m == k).int() * act
@@ -193,6 +196,6 @@ class SpecDecEngine:
         return self.out[:, :self.max_new]
 
     def acceptance(self) -> float:
-        """Mean accepted candidates per round and sequence (the rounds a sequence was frozen
-        for count as rounds with nothing accepted)."""
-        return float(self.accepted.sum()) / max(1, self.rounds * self.B)
+        """Mean accepted candidates per round and sequence, over the rounds each sequence
+        was active in (not frozen)."""
+        return float(self.accepted.sum()) / max(1, int(self.active_rounds.sum()))
