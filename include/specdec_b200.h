@@ -60,6 +60,7 @@ typedef enum SpecdecResult {
 #define SPECDEC_STATUS_TRIM_RANGE 0x8    /* trim length <= 0 or > current length      */
 #define SPECDEC_STATUS_TIMEOUT 0x10      /* a bounded device wait gave up             */
 #define SPECDEC_STATUS_ACCEPT_RANGE 0x20 /* accept: kp outside [1, max_cands]         */
+#define SPECDEC_STATUS_PLAN_MISMATCH 0x40 /* reused plan built for another launch shape */
 
 typedef enum SpecdecDtype { SPECDEC_F32 = 0, SPECDEC_BF16 = 1, SPECDEC_E4M3 = 2 } SpecdecDtype;
 
@@ -135,7 +136,12 @@ typedef struct SpecdecAttnArgs {
      of them.  The kernel then starts loading them while that work finishes (Q is
      still read, and outputs written, only after it).  0: nothing is read early. */
   int32_t history_ready;
-  int32_t reserved0;
+  /* Thread-block clusters for small batches: 0 = the library's choice (when every
+     (sequence, query tile, KV head) group of the batch gets clusters of its own, the
+     CTAs of a cluster reduce their split partials through distributed shared memory);
+     1 = never; 8 or 16 = clusters of that many CTAs when the batch fits.  The plan
+     (specdec_ragged_plan) and the attention calls that reuse it must pass the same value. */
+  int32_t cluster_size;
 } SpecdecAttnArgs;
 
 /* Bytes of workspace (plan + split-KV partials) for a batch of this shape. */

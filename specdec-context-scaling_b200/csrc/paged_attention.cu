@@ -53,8 +53,12 @@ struct CtaDesc {
   int32_t pages[32];
   // the plan header's merge counts and CTA count, so the merge needs no header load
   int32_t num_merge_wide, num_merge_narrow, num_ctas;
-  int32_t pad1[13];
+  // the launch shape the plan was built for: the verify kernel runs nothing when the
+  // descriptor does not match its own grid (a plan reused with another cluster choice)
+  int32_t plan_magic, plan_cluster, plan_grid;
+  int32_t pad1[10];
 };
+constexpr int32_t kPlanMagic = 0x53504c4e;
 static_assert(sizeof(CtaDesc) == 256, "CTA descriptor is 256 bytes");
 struct GroupInfo {
   int32_t first_item, nsplit, b, h, q0, nq, pad0, pad1;
@@ -272,6 +276,9 @@ SD_DEV void cluster_plan(const AttnParams& p) {
     d.num_merge_wide = 0;
     d.num_merge_narrow = 0;
     d.num_ctas = grid;
+    d.plan_magic = kPlanMagic;
+    d.plan_cluster = CS;
+    d.plan_grid = grid;
   }
   __syncthreads();
   for (int u = t; u < grid * 32; u += blockDim.x) {
@@ -469,6 +476,11 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
     p.cdesc[bx].num_merge_wide = wcarry;
     p.cdesc[bx].num_merge_narrow = ncarry;
     p.cdesc[bx].num_ctas = C;
+    p.cdesc[bx].cl_first = 0;
+    p.cdesc[bx].cl_count = 0;
+    p.cdesc[bx].plan_magic = kPlanMagic;
+    p.cdesc[bx].plan_cluster = 0;
+    p.cdesc[bx].plan_grid = grid;
   }
   // first item and page ids: thread t fills page slot t % 32 of CTA t / 32
   for (int u = threadIdx.x; u < C * 32; u += blockDim.x) {
@@ -977,12 +989,74 @@ static int launch_verify(const AttnParams& p, const CUtensorMap& kmap, const CUt
                          const CUtensorMap& smap, cudaStream_t st,
                          bool pdl) {
   using Geo = V3Geom<NR < 16 ? 16 : NR, VF8, D>;
+  if (p.cluster_size > 0) {
+    // cluster mode: num_clusters clusters of cluster_size CTAs, one item per CTA
+    auto kern = verify_kernel<NR, VF8, TMAP, D, PP, true>;
+    static bool attr[64] = {};
+    set_smem_attr(kern, Geo::SMEM, attr);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.num_clusters * p.cluster_size);
+    cfg.blockDim = dim3(v3_threads<VF8>());
+    cfg.dynamicSmemBytes = Geo::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = static_cast<unsigned>(p.cluster_size);
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 2 : 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p, kmap, vmap, smap);
+    if (e != cudaSuccess) return fail(SPECDEC_ERR_CUDA, "verify_kernel (clusters) launch: %s", cudaGetErrorString(e));
+    return after_launch("verify_kernel");
+  }
   static bool attr[64] = {};
-  set_smem_attr(verify_kernel<NR, VF8, TMAP, D, PP>, Geo::SMEM, attr);
+  set_smem_attr(verify_kernel<NR, VF8, TMAP, D, PP, false>, Geo::SMEM, attr);
   // persistent: one CTA per SM, the plan's C = target_items / 4 ranges
   const int grid = p.target_items / 4;
-  return launch_k("verify_kernel", verify_kernel<NR, VF8, TMAP, D, PP>, dim3(grid), dim3(v3_threads<VF8>()), Geo::SMEM, st,
-                  pdl, p, kmap, vmap, smap);
+  return launch_k("verify_kernel", verify_kernel<NR, VF8, TMAP, D, PP, false>, dim3(grid), dim3(v3_threads<VF8>()),
+                  Geo::SMEM, st, pdl, p, kmap, vmap, smap);
+}
+
+// Clusters of `cs` CTAs of this verify kernel that can be resident at once (cached per
+// device); 0 when the device cannot run such clusters.
+template <int NR, bool VF8, bool TMAP, int D, bool PP>
+static int resident_clusters(int cs) {
+  using Geo = V3Geom<NR < 16 ? 16 : NR, VF8, D>;
+  static int cache[64][2] = {};
+  static bool known[64][2] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  const int ci = cs == 16 ? 1 : 0;
+  if (known[dev][ci]) return cache[dev][ci];
+  auto kern = verify_kernel<NR, VF8, TMAP, D, PP, true>;
+  static bool attr[64] = {};
+  set_smem_attr(kern, Geo::SMEM, attr);
+  if (cs > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+    cudaGetLastError();
+    known[dev][ci] = true;
+    return cache[dev][ci] = 0;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cs);
+  cfg.blockDim = dim3(v3_threads<VF8>());
+  cfg.dynamicSmemBytes = Geo::SMEM;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = static_cast<unsigned>(cs);
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  known[dev][ci] = true;
+  return cache[dev][ci] = n;
 }
 
 // CTAs of the persistent verify kernel: the caller's SM budget, at most the device's
@@ -1037,6 +1111,39 @@ static int run_attention(AttnParams p, const CUtensorMap& kmap, const CUtensorMa
   return record_event(ev_end, stream);
 }
 
+// Cluster mode for small batches: every group of the batch (sequence x query tile x KV head)
+// gets clusters of its own, so the split reduction stays inside clusters (distributed shared
+// memory) instead of a grid barrier and a global merge.  `hint`: 0 the library's choice
+// (clusters of 16, else 8), 1 no clusters, 8 or 16 that size.  Sets p.cluster_size and
+// p.num_clusters (0 = the persistent grid).
+template <int NR, bool VF8, bool TMAP, int D, bool PP>
+static void choose_clusters_nr(AttnParams& p, int hint, int sms) {
+  p.cluster_size = 0;
+  p.num_clusters = 0;
+  if (hint == 1 || p.max_groups > kClusterMaxGroups) return;
+  const int sizes[2] = {16, 8};
+  for (int cs : sizes) {
+    if (hint != 0 && hint != cs) continue;
+    const int nc = std::min(resident_clusters<NR, VF8, TMAP, D, PP>(cs), sms / cs);
+    if (nc >= p.max_groups && nc > 0) {
+      p.cluster_size = cs;
+      p.num_clusters = nc;
+      return;
+    }
+  }
+}
+
+template <int D, bool VF8, bool TMAP>
+static void choose_clusters(AttnParams& p, int hint, int sms) {
+  const int rows_max = p.n_rep * (p.q_tile < p.max_q_len ? p.q_tile : p.max_q_len);
+  if (rows_max <= 8)
+    choose_clusters_nr<8, VF8, TMAP, D, true>(p, hint, sms);
+  else if (rows_max <= 16)
+    choose_clusters_nr<16, VF8, TMAP, D, kTwoGroup16>(p, hint, sms);
+  else
+    choose_clusters_nr<32, VF8, TMAP, D, kTwoGroup32>(p, hint, sms);
+}
+
 static int fill_workspace(AttnParams& p, void* ws, size_t ws_bytes, int B, int KV, int D, int num_sms, int occ) {
   const int target = target_items_for(num_sms, occ);
   const WsLayout w = ws_layout(B, KV, p.max_qtiles, D, target);
@@ -1051,6 +1158,7 @@ static int fill_workspace(AttnParams& p, void* ws, size_t ws_bytes, int B, int K
   p.cta_first = reinterpret_cast<int32_t*>(base + w.ctas);
   p.cdesc = reinterpret_cast<CtaDesc*>(base + w.cdesc);
   p.merge_list = reinterpret_cast<GroupInfo*>(base + w.mlist);
+  p.tickets = reinterpret_cast<int32_t*>(base + w.tickets);
   p.p_stat = reinterpret_cast<float*>(base + w.lse);
   p.p_o = reinterpret_cast<float*>(base + w.po);
   p.max_items = w.max_items;
@@ -1135,6 +1243,17 @@ static int paged_entry(const SpecdecAttnArgs* a, cudaStream_t stream, bool plan_
   const int sms = sm_budget(a->num_sms);
   if (int rc = fill_workspace(p, a->workspace, a->workspace_bytes, p.B, p.KV, D, sms, occupancy_for(D, vf8, false)))
     return rc;
+  const int hint = a->cluster_size;
+  if (hint != 0 && hint != 1 && hint != 8 && hint != 16)
+    return fail(SPECDEC_ERR_INVALID, "cluster_size must be 0 (automatic), 1 (none), 8 or 16");
+  if (D == 128) {
+    if (vf8)
+      choose_clusters<128, true, false>(p, hint, sms);
+    else
+      choose_clusters<128, false, false>(p, hint, sms);
+  } else {
+    choose_clusters<64, false, false>(p, hint, sms);
+  }
   if (plan_only) {
     plan_kernel<<<1, 1024, 0, stream>>>(p);
     return after_launch("plan_kernel");
@@ -1322,6 +1441,10 @@ extern "C" int specdec_attention(const void* q, const void* k, const void* v, vo
   p.scale_log2 = (1.0f / sqrtf(static_cast<float>(D))) * 1.4426950408889634f;
   const int sms = device_sm_count();
   if (int rc = fill_workspace(p, workspace, workspace_bytes, B, KV, D, sms, occupancy_for(D, false, true))) return rc;
+  if (D == 128)
+    choose_clusters<128, false, true>(p, 0, sms);
+  else
+    choose_clusters<64, false, true>(p, 0, sms);
   CUtensorMap kmap, vmap;
   if (int rc = encode_kv_map(&kmap, k, B * KV, T, D)) return rc;
   if (int rc = encode_kv_map(&vmap, v, B * KV, T, D)) return rc;

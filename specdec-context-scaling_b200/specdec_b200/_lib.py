@@ -29,6 +29,7 @@ STATUS_BAD_PAGE = 0x4
 STATUS_TRIM_RANGE = 0x8
 STATUS_TIMEOUT = 0x10
 STATUS_ACCEPT_RANGE = 0x20
+STATUS_PLAN_MISMATCH = 0x40
 
 STATUS_NAMES = {
     STATUS_BAD_LENGTH: "bad length (ctx_len < q_len or q_len > max_q_len)",
@@ -37,6 +38,7 @@ STATUS_NAMES = {
     STATUS_TRIM_RANGE: "trim length out of range",
     STATUS_TIMEOUT: "bounded device wait timed out",
     STATUS_ACCEPT_RANGE: "accept row/candidate count out of range",
+    STATUS_PLAN_MISMATCH: "reused plan was built for another launch shape (cluster choice or SM budget)",
 }
 
 _vp = ctypes.c_void_p
@@ -89,7 +91,7 @@ class AttnArgs(ctypes.Structure):
         ("split_event_begin", _vp),
         ("split_event_end", _vp),
         ("history_ready", _i32),
-        ("reserved0", _i32),
+        ("cluster_size", _i32),
     ]
 
 

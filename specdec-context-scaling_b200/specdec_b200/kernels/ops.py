@@ -248,12 +248,15 @@ def _paged_kv(cache: PagedKVCache, layer: int) -> _lib.PagedKV:
 
 def attn_args(q: torch.Tensor, out: torch.Tensor, cache: PagedKVCache, layer: int, batch: RaggedBatch,
               workspace: torch.Tensor, *, sm_scale: float | None = None, status: torch.Tensor | None = None,
-              reuse_plan: bool = False, split_events=None, history_ready: bool = False) -> _lib.AttnArgs:
+              reuse_plan: bool = False, split_events=None, history_ready: bool = False,
+              cluster_size: int = 0) -> _lib.AttnArgs:
     """Pack the C argument struct of one paged attention call (reusable across calls).
 
     ``history_ready``: the caller promises that the KV history (positions below
     ctx_len - q_len), the page table and the reused plan are not written by the work
-    right before this call on the stream, so the kernel may load them early."""
+    right before this call on the stream, so the kernel may load them early.
+    ``cluster_size``: 0 the library's choice of thread-block clusters for small batches,
+    1 none, 8 or 16 clusters of that size (a plan and the calls reusing it agree)."""
     if q.dim() != 3 or q.dtype != torch.bfloat16:
         raise ValueError("q must be bf16 (total_rows, num_q_heads, head_dim)")
     if q.shape[2] != cache.head_dim:
@@ -287,7 +290,7 @@ def attn_args(q: torch.Tensor, out: torch.Tensor, cache: PagedKVCache, layer: in
         split_event_begin=None if split_events is None else _event_handle(split_events[0]),
         split_event_end=None if split_events is None else _event_handle(split_events[1]),
         history_ready=1 if history_ready else 0,
-        reserved0=0,
+        cluster_size=int(cluster_size),
     )
 
 
@@ -298,15 +301,16 @@ def _event_handle(ev: torch.cuda.Event) -> int:
     return ev.cuda_event
 
 
-def ragged_plan(q, cache: PagedKVCache, batch: RaggedBatch, workspace: torch.Tensor, *, status=None) -> None:
+def ragged_plan(q, cache: PagedKVCache, batch: RaggedBatch, workspace: torch.Tensor, *, status=None,
+                cluster_size: int = 0) -> None:
     """Build the split-KV work list for ``batch`` in ``workspace`` on the device (no host sync)."""
-    args = attn_args(q, q, cache, 0, batch, workspace, status=status)
+    args = attn_args(q, q, cache, 0, batch, workspace, status=status, cluster_size=cluster_size)
     _lib.check(_lib_handle().specdec_ragged_plan(ctypes.byref(args), _stream()), "ragged_plan")
 
 
 def paged_attention(q, cache: PagedKVCache, layer: int, batch: RaggedBatch, *, out=None, workspace=None,
                     sm_scale=None, status=None, reuse_plan: bool = False, split_events=None,
-                    history_ready: bool = False):
+                    history_ready: bool = False, cluster_size: int = 0):
     """Decode / verify / ragged attention of packed query rows ``q`` (rows, H, D) over layer ``layer``.
 
     ``split_events`` (optional pair of torch.cuda.Event with timing) brackets the split-KV kernel."""
@@ -318,7 +322,8 @@ def paged_attention(q, cache: PagedKVCache, layer: int, batch: RaggedBatch, *, o
         workspace = attn_workspace(batch, q.shape[1], cache)
         reuse_plan = False
     args = attn_args(q, out, cache, layer, batch, workspace, sm_scale=sm_scale, status=status,
-                     reuse_plan=reuse_plan, split_events=split_events, history_ready=history_ready)
+                     reuse_plan=reuse_plan, split_events=split_events, history_ready=history_ready,
+                     cluster_size=cluster_size)
     _lib.check(_lib_handle().specdec_paged_attention(ctypes.byref(args), _stream()), "paged_attention")
     return out
 

@@ -230,6 +230,68 @@ def test_draft_decode_full_size():
     assert_close_attention(got, oracle_rows(q, ks, vrefs, q_lens), "draft decode 64 x 8K")
 
 
+@pytest.mark.parametrize("cluster_size", [1, 8, 16])
+@pytest.mark.parametrize("lens,q_lens,fp8,H,D", [
+    ([8192], [5], False, 12, 128),
+    ([8192], [1], True, 12, 128),
+    ([4096], [5], True, 12, 128),
+    ([2048], [2], False, 14, 64),
+    ([100], [5], False, 12, 128),
+    ([5], [5], True, 12, 128),
+    ([3000, 77, 1, 640], [5, 1, 5, 2], True, 12, 128),
+    ([8192, 0, 2500], [1, 0, 1], False, 14, 64),
+])
+def test_small_batches_on_clusters(cluster_size, lens, q_lens, fp8, H, D):
+    """Small batches with every (sequence, query tile, KV head) group on thread-block clusters
+    of its own (8 or 16 CTAs: the split partials reduced in distributed shared memory, groups
+    spread over several clusters joined by per-row tickets) and on the persistent grid (1),
+    against the oracle; a plan reused by the following calls of a step gives the same rows."""
+    ops = _ops()
+    lens = [max(n, q) for n, q in zip(lens, q_lens)]
+    lens_cache = [max(n, 1) for n in lens]
+    cache, ks, vrefs = build_cache(lens_cache, 2, D, fp8=fp8, seed=sum(lens) + cluster_size, num_layers=2)
+    batch = ops.RaggedBatch.from_lengths(q_lens, lens)
+    q = torch.randn(batch.total_rows, H, D, generator=torch.Generator().manual_seed(7)).to(torch.bfloat16)
+    qc = q.cuda()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ws = ops.attn_workspace(batch, H, cache)
+    ops.ragged_plan(qc, cache, batch, ws, status=status, cluster_size=cluster_size)
+    outs = [ops.paged_attention(qc, cache, layer, batch, workspace=ws, reuse_plan=True, status=status,
+                                history_ready=layer > 0, cluster_size=cluster_size) for layer in range(2)]
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    keep = [i for i, n in enumerate(q_lens) if n > 0]
+    row0 = [sum(q_lens[:i]) for i in range(len(q_lens))]
+    rows = torch.cat([torch.arange(row0[i], row0[i] + q_lens[i]) for i in keep])
+    ref = oracle_rows(q[rows], [ks[i] for i in keep], [vrefs[i] for i in keep], [q_lens[i] for i in keep])
+    for o in outs:
+        assert_close_attention(o.cpu()[rows], ref, f"clusters={cluster_size} lens={lens} q={q_lens}")
+    assert torch.equal(outs[0], outs[1])
+
+
+def test_plan_built_for_another_launch_shape_is_refused():
+    """A plan reused by a call that would launch another grid (clusters of 8 against clusters
+    of 16, or the persistent grid) is detected on the device: the call sets
+    SPECDEC_STATUS_PLAN_MISMATCH and computes nothing, in every CTA alike."""
+    from specdec_b200 import _lib
+
+    ops = _ops()
+    cache, ks, vrefs = build_cache([4096], 2, 128, fp8=False, seed=3)
+    batch = ops.RaggedBatch.from_lengths([5], [4096])
+    q = torch.randn(5, 12, 128, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16).cuda()
+    ws = ops.attn_workspace(batch, 12, cache)
+    for planned, used in ((8, 16), (16, 1), (1, 8)):
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        ops.ragged_plan(q, cache, batch, ws, cluster_size=planned)
+        ops.paged_attention(q, cache, 0, batch, workspace=ws, reuse_plan=True, status=status, cluster_size=used)
+        torch.cuda.synchronize()
+        assert int(status.item()) & _lib.STATUS_PLAN_MISMATCH, (planned, used)
+    # and the matching plan still works afterwards
+    ops.ragged_plan(q, cache, batch, ws, cluster_size=16)
+    out = ops.paged_attention(q, cache, 0, batch, workspace=ws, reuse_plan=True, cluster_size=16)
+    assert_close_attention(out.cpu(), oracle_rows(q.cpu(), ks, vrefs, [5]), "matching plan")
+
+
 def test_plan_reuse_across_layers():
     """One plan serves every layer: reuse_plan=True gives the same output as a fresh plan."""
     ops = _ops()
