@@ -42,7 +42,7 @@ extern "C" {
 
 typedef struct CUstream_st* specdec_stream_t; /* == cudaStream_t */
 
-#define SPECDEC_ABI_VERSION 2
+#define SPECDEC_ABI_VERSION 3
 #define SPECDEC_PAGE_TOKENS 16 /* tokens per KV page */
 
 typedef enum SpecdecResult {
@@ -107,6 +107,8 @@ typedef struct SpecdecBatch {
   int32_t num_seqs;
   int32_t num_q_heads;
   int32_t max_q_len; /* upper bound of q_len[], host-known; sizes the plan */
+  int32_t max_ctx_len; /* upper bound of ctx_len[] when the host knows one, else 0; a small batch
+                          of short contexts then runs on thread-block clusters (cluster_size) */
 } SpecdecBatch;
 
 typedef struct SpecdecAttnArgs {
@@ -136,11 +138,13 @@ typedef struct SpecdecAttnArgs {
      of them.  The kernel then starts loading them while that work finishes (Q is
      still read, and outputs written, only after it).  0: nothing is read early. */
   int32_t history_ready;
-  /* Thread-block clusters for small batches: 0 = the library's choice (when every
-     (sequence, query tile, KV head) group of the batch gets clusters of its own, the
-     CTAs of a cluster reduce their split partials through distributed shared memory);
-     1 = never; 8 or 16 = clusters of that many CTAs when the batch fits.  The plan
-     (specdec_ragged_plan) and the attention calls that reuse it must pass the same value. */
+  /* Thread-block clusters for small batches: the CTAs of a cluster reduce their split
+     partials through distributed shared memory instead of a grid barrier and a merge
+     through global memory.  0 = the library's choice: clusters when batch.max_ctx_len is
+     known and every (sequence, query tile, KV head) group fits one cluster at one 128-key
+     tile per CTA; 1 = never; 8 or 16 = clusters of that many CTAs whenever every group gets
+     clusters of its own.  The plan (specdec_ragged_plan) and the attention calls that reuse
+     it must pass the same value (a mismatch is refused: SPECDEC_STATUS_PLAN_MISMATCH). */
   int32_t cluster_size;
 } SpecdecAttnArgs;
 
@@ -152,6 +156,11 @@ size_t specdec_attn_workspace_bytes(int32_t num_seqs, int32_t num_q_heads, int32
    The attention call with reuse_plan=1 consumes it; one plan serves every layer
    that shares the batch's lengths. */
 int specdec_ragged_plan(const SpecdecAttnArgs* args, specdec_stream_t stream);
+
+/* The launch shape specdec_paged_attention would use for these arguments (host-only, no
+   launch): the verify kernel's grid and its cluster size (0: the persistent grid, no
+   clusters).  No counterpart in the reference. */
+int specdec_attn_launch_shape(const SpecdecAttnArgs* args, int32_t* grid, int32_t* cluster_size);
 
 /* Paged decode (q_len 1) / block-verify (q_len k+1) / ragged attention. */
 int specdec_paged_attention(const SpecdecAttnArgs* args, specdec_stream_t stream);

@@ -135,6 +135,7 @@ struct AttnParams {
   // memory; groups spread over several clusters meet through per-row tickets
   int32_t cluster_size, num_clusters;
   int32_t* tickets;  // [num_clusters][kMaxRows]: arrivals of a group's clusters per row
+  int32_t max_ctx_hint;  // host-known upper bound of the context lengths, 0 when unknown
 };
 
 SD_DEV int seq_q_len(const AttnParams& p, int b) { return p.q_len ? p.q_len[b] : p.uni_q_len; }
@@ -205,6 +206,7 @@ SD_DEV int block_exclusive_scan(int v, int& total, int* s_warp) {
 // come first in the grid (dispatched first, they leave at once).  One item per CTA, item
 // index = block index.  The per-row tickets of the clusters start at zero.
 constexpr int kClusterMaxGroups = 32;
+constexpr int kClusterMaxSlots = 8;  // clusters a group may span (the last one merges that many partials)
 SD_DEV void cluster_plan(const AttnParams& p) {
   __shared__ int s_pages[kClusterMaxGroups], s_c[kClusterMaxGroups], s_cl0[kClusterMaxGroups];
   const int G = p.max_groups, CS = p.cluster_size, NC = p.num_clusters, grid = NC * CS;
@@ -215,14 +217,17 @@ SD_DEV void cluster_plan(const AttnParams& p) {
   }
   __syncthreads();
   if (t == 0) {
+    // (a group spans at most kClusterMaxSlots clusters: the last one merges that many partials)
     int k = 1;
     for (;; ++k) {
-      int need = 0;
+      int need = 0, widest = 0;
       for (int g = 0; g < G; ++g) {
         const int tiles = (s_pages[g] + kPlanTilePages - 1) / kPlanTilePages;
-        need += (tiles + CS * k - 1) / (CS * k);
+        const int c = (tiles + CS * k - 1) / (CS * k);
+        need += c;
+        widest = max(widest, c);
       }
-      if (need <= NC) break;
+      if (need <= NC && widest <= kClusterMaxSlots) break;
     }
     int used = 0;
     for (int g = 0; g < G; ++g) {
@@ -690,54 +695,73 @@ SD_DEV bool grid_barrier(unsigned long long* counter, unsigned n_ctas, bool wait
 // the statistics (row max, four key-quarter sums at cl_st + row * kStatStride); a CTA
 // without pages holds zero rows with max -inf.  After a cluster barrier, CTA rank cr owns
 // rows cr, cr + CS, ... and combines the CS partials of each through distributed shared
-// memory (warps take the (row, peer) units in turn; states combined max-first in this CTA's
-// scratch `s_st`, which no peer reads).  A group on one cluster writes the output row; a
-// group on c > 1 clusters writes the cluster's partial of the row to the workspace
-// (slot = cluster index), and the row's last-arriving cluster (per-row ticket, counted
-// after a release fence) combines the c partials, writes the output and resets the ticket.
-constexpr int kClusterMaxOwn = 4;  // rows per CTA: at most 32 rows over clusters of >= 8 CTAs
+// memory: every warp issues the loads of all its (row, peer) units at once, then combines
+// them max-first; the warps' states meet in this CTA's scratch `s_st` (no peer reads it).
+// Once its loads are in, the CTA arrives on the cluster's exit barrier, so peers never wait
+// for its global work.  A group on one cluster writes the output row; a group on c > 1
+// clusters writes the cluster's partial of the row to the workspace (slot = cluster
+// index), and the row's last-arriving cluster (per-row ticket, counted after a release
+// fence) combines the c partials, writes the output and resets the ticket.
+constexpr int kClusterMaxOwn = 4;   // rows per CTA: at most 32 rows over clusters of >= 8 CTAs
+constexpr int kClusterMaxUnits = 4;  // (row, peer) units per warp step: 32 units over >= 8 warps
 
 template <int D, int NWARP>
 SD_DEV void cluster_merge(const AttnParams& p, const CtaDesc& cd, const float* cl_o, const float* cl_st,
                           MergeState* s_st, int warp, int lane) {
   constexpr int NQ = D / 4;     // dim quads: lanes per row
   constexpr int SPW = 32 / NQ;  // units per warp step
+  // a CTA has at most 32 units: 32 rows over clusters of 8 or 16 CTAs
+  static_assert(NWARP * SPW * kClusterMaxUnits >= 32, "units of a CTA in one step");
   const int quad = lane % NQ, slot = lane / NQ;
   const int CS = static_cast<int>(cluster_nctarank()), cr = static_cast<int>(cluster_ctarank());
   const WorkItem& g = cd.first;
   const int R = p.n_rep * g.nq;
   const int own = R > cr ? (R - cr + CS - 1) / CS : 0;  // rows cr, cr + CS, ...
+  const int units = own * CS;
   const uint32_t o_base = smem_u32(cl_o), st_base = smem_u32(cl_st);
 
-  MergeState st[kClusterMaxOwn];
+  // all loads of this lane's units first (unit u = warp * SPW + slot + k * NWARP * SPW)
+  float4 s4[kClusterMaxUnits], o4[kClusterMaxUnits];
+  float l3[kClusterMaxUnits];
+  int ju[kClusterMaxUnits];
 #pragma unroll
-  for (int j = 0; j < kClusterMaxOwn; ++j) {
-    st[j].m = -INFINITY;
-    st[j].l = 0.f;
-    st[j].a = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  const int units = own * CS;
-  for (int u0 = warp * SPW; u0 < units; u0 += NWARP * SPW) {
-    const int u = u0 + slot;
+  for (int k = 0; k < kClusterMaxUnits; ++k) {
+    const int u = warp * SPW + slot + k * NWARP * SPW;
+    ju[k] = -1;
     if (u < units) {
       const int j = u / CS, peer = u - j * CS;
       const int row = cr + j * CS;
-      const float4 s4 = dsmem_ld4(dsmem_addr(st_base + row * kStatStride * 4, peer));
-      const float l3 = dsmem_ld(dsmem_addr(st_base + (row * kStatStride + 4) * 4, peer));
-      MergeState o;
-      o.m = s4.x;
-      o.l = (s4.y + s4.z) + (s4.w + l3);
-      o.a = dsmem_ld4(dsmem_addr(o_base + (row * D + 4 * quad) * 4, peer));
-#pragma unroll
-      for (int jj = 0; jj < kClusterMaxOwn; ++jj)
-        if (jj == j) merge_combine(st[jj], o);
+      ju[k] = j;
+      s4[k] = dsmem_ld4(dsmem_addr(st_base + row * kStatStride * 4, peer));
+      l3[k] = dsmem_ld(dsmem_addr(st_base + (row * kStatStride + 4) * 4, peer));
+      o4[k] = dsmem_ld4(dsmem_addr(o_base + (row * D + 4 * quad) * 4, peer));
     }
   }
-  // the warp's two unit slots (head_dim 64) hold different units of possibly the same row:
-  // fold slot 1 into slot 0 row by row, then publish the warp's states
+  // per row: the max of this lane's units first, then independent weights
+  MergeState st[kClusterMaxOwn];
 #pragma unroll
   for (int j = 0; j < kClusterMaxOwn; ++j) {
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < kClusterMaxUnits; ++k)
+      if (ju[k] == j) m = fmaxf(m, s4[k].x);
+    st[j].m = m;
+    st[j].l = 0.f;
+    st[j].a = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (m != -INFINITY) {
+#pragma unroll
+      for (int k = 0; k < kClusterMaxUnits; ++k) {
+        if (ju[k] != j) continue;
+        const float w = fast_exp2(s4[k].x - m);  // 0 for an empty partial (-inf)
+        st[j].l += ((s4[k].y + s4[k].z) + (s4[k].w + l3[k])) * w;
+        st[j].a.x += o4[k].x * w;
+        st[j].a.y += o4[k].y * w;
+        st[j].a.z += o4[k].z * w;
+        st[j].a.w += o4[k].w * w;
+      }
+    }
     if (SPW == 2) {
+      // head_dim 64: the warp's two unit slots, folded into slot 0
       MergeState o;
       o.m = __shfl_xor_sync(0xffffffffu, st[j].m, 16);
       o.l = __shfl_xor_sync(0xffffffffu, st[j].l, 16);
@@ -749,20 +773,21 @@ SD_DEV void cluster_merge(const AttnParams& p, const CtaDesc& cd, const float* c
     }
     if (j < own) s_st[(j * NWARP + warp) * 32 + lane] = st[j];
   }
-  __syncthreads();
+  __syncthreads();  // every DSMEM load of this CTA has returned
+  cluster_arrive();  // the peers may leave once they are done too
   if (warp >= own || slot != 0) return;
   // warp j finishes row cr + j * CS: the warps' states, common max first
   const int j = warp, row = cr + j * CS;
   MergeState tot;
   {
     float m = -INFINITY;
-#pragma unroll 1
+#pragma unroll
     for (int w = 0; w < NWARP; ++w) m = fmaxf(m, s_st[(j * NWARP + w) * 32 + lane].m);
     tot.m = m;
     tot.l = 0.f;
     tot.a = make_float4(0.f, 0.f, 0.f, 0.f);
     if (m != -INFINITY) {
-#pragma unroll 1
+#pragma unroll
       for (int w = 0; w < NWARP; ++w) {
         const MergeState o = s_st[(j * NWARP + w) * 32 + lane];
         const float wt = fast_exp2(o.m - m);
@@ -794,17 +819,34 @@ SD_DEV void cluster_merge(const AttnParams& p, const CtaDesc& cd, const float* c
     last = __shfl_sync(lanes, last, 0);
     if (!last) return;
     __threadfence();
-    tot.m = -INFINITY;
+    float ms[kClusterMaxSlots], ls[kClusterMaxSlots];
+    float4 os[kClusterMaxSlots];
+#pragma unroll
+    for (int c = 0; c < kClusterMaxSlots; ++c) {
+      ms[c] = -INFINITY;
+      ls[c] = 0.f;
+      os[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c < cd.cl_count) {
+        const int64_t sr = static_cast<int64_t>(cd.cl_first + c) * kMaxRows + row;
+        ms[c] = __ldcg(p.p_stat + sr * kStatStride);
+        ls[c] = __ldcg(p.p_stat + sr * kStatStride + 1);
+        os[c] = __ldcg(reinterpret_cast<const float4*>(p.p_o + sr * D) + quad);
+      }
+    }
+    float m = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < kClusterMaxSlots; ++c) m = fmaxf(m, ms[c]);
+    tot.m = m;
     tot.l = 0.f;
     tot.a = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 1
-    for (int c = 0; c < cd.cl_count; ++c) {
-      const int64_t sr = static_cast<int64_t>(cd.cl_first + c) * kMaxRows + row;
-      MergeState o;
-      o.m = __ldcg(p.p_stat + sr * kStatStride);
-      o.l = __ldcg(p.p_stat + sr * kStatStride + 1);
-      o.a = __ldcg(reinterpret_cast<const float4*>(p.p_o + sr * D) + quad);
-      merge_combine(tot, o);
+#pragma unroll
+    for (int c = 0; c < kClusterMaxSlots; ++c) {
+      const float wt = ms[c] == -INFINITY ? 0.f : fast_exp2(ms[c] - m);
+      tot.l += ls[c] * wt;
+      tot.a.x += os[c].x * wt;
+      tot.a.y += os[c].y * wt;
+      tot.a.z += os[c].z * wt;
+      tot.a.w += os[c].w * wt;
     }
     if (quad == 0) p.tickets[static_cast<int64_t>(cd.cl_first) * kMaxRows + row] = 0;
   }
@@ -1090,6 +1132,9 @@ static int record_event(void* ev, cudaStream_t stream) {
 // group on every tile with the rows split in halves (false)
 constexpr bool kTwoGroup16 = true;
 constexpr bool kTwoGroup32 = false;
+// in cluster mode a CTA takes at most a few tiles: two groups on alternate tiles run them
+// side by side
+constexpr bool kTwoGroup32Clusters = false;
 
 template <int D, bool VF8, bool TMAP>
 static int run_attention(AttnParams p, const CUtensorMap& kmap, const CUtensorMap& vmap, const CUtensorMap& smap,
@@ -1106,7 +1151,9 @@ static int run_attention(AttnParams p, const CUtensorMap& kmap, const CUtensorMa
   const int rows_max = p.n_rep * (p.q_tile < p.max_q_len ? p.q_tile : p.max_q_len);
   const int rc = rows_max <= 8    ? launch_verify<8, VF8, TMAP, D, true>(p, kmap, vmap, smap, stream, pdl)
                  : rows_max <= 16 ? launch_verify<16, VF8, TMAP, D, kTwoGroup16>(p, kmap, vmap, smap, stream, pdl)
-                                  : launch_verify<32, VF8, TMAP, D, kTwoGroup32>(p, kmap, vmap, smap, stream, pdl);
+                 : p.cluster_size > 0
+                     ? launch_verify<32, VF8, TMAP, D, kTwoGroup32Clusters>(p, kmap, vmap, smap, stream, pdl)
+                     : launch_verify<32, VF8, TMAP, D, kTwoGroup32>(p, kmap, vmap, smap, stream, pdl);
   if (rc) return rc;
   return record_event(ev_end, stream);
 }
@@ -1116,14 +1163,23 @@ static int run_attention(AttnParams p, const CUtensorMap& kmap, const CUtensorMa
 // memory) instead of a grid barrier and a global merge.  `hint`: 0 the library's choice
 // (clusters of 16, else 8), 1 no clusters, 8 or 16 that size.  Sets p.cluster_size and
 // p.num_clusters (0 = the persistent grid).
+// The library's own choice (hint 0) takes clusters only where they are measured to win:
+// every group on one cluster with at most one 128-key tile per CTA (no cross-cluster step,
+// no second tile), which needs the host's bound on the context length.  On this B200 at
+// most 7 clusters of 16 and 15 of 8 CTAs are resident, so an 8192-token sequence (64 tiles
+// per KV head) would need two tiles per CTA or several clusters per group; the persistent
+// grid (128 CTAs of one tile) is faster there.
 template <int NR, bool VF8, bool TMAP, int D, bool PP>
 static void choose_clusters_nr(AttnParams& p, int hint, int sms) {
   p.cluster_size = 0;
   p.num_clusters = 0;
   if (hint == 1 || p.max_groups > kClusterMaxGroups) return;
+  if (hint == 0 && p.max_ctx_hint <= 0) return;
+  const int tiles_max = (p.max_ctx_hint + kPlanTilePages * kPage - 1) / (kPlanTilePages * kPage);
   const int sizes[2] = {16, 8};
   for (int cs : sizes) {
     if (hint != 0 && hint != cs) continue;
+    if (hint == 0 && tiles_max > cs) continue;
     const int nc = std::min(resident_clusters<NR, VF8, TMAP, D, PP>(cs), sms / cs);
     if (nc >= p.max_groups && nc > 0) {
       p.cluster_size = cs;
@@ -1141,7 +1197,7 @@ static void choose_clusters(AttnParams& p, int hint, int sms) {
   else if (rows_max <= 16)
     choose_clusters_nr<16, VF8, TMAP, D, kTwoGroup16>(p, hint, sms);
   else
-    choose_clusters_nr<32, VF8, TMAP, D, kTwoGroup32>(p, hint, sms);
+    choose_clusters_nr<32, VF8, TMAP, D, kTwoGroup32Clusters>(p, hint, sms);
 }
 
 static int fill_workspace(AttnParams& p, void* ws, size_t ws_bytes, int B, int KV, int D, int num_sms, int occ) {
@@ -1232,6 +1288,7 @@ static AttnParams params_from(const SpecdecAttnArgs* a) {
   p.max_pages = a->kv.max_pages_per_seq;
   p.scale_log2 = a->sm_scale * 1.4426950408889634f;
   p.status = a->status;
+  p.max_ctx_hint = a->batch.max_ctx_len;
   return p;
 }
 
@@ -1298,6 +1355,31 @@ extern "C" size_t specdec_attn_workspace_bytes(int32_t num_seqs, int32_t num_q_h
   // occupancy is not known without a device query; size for 4 CTAs per SM (an upper bound)
   const int target = target_items_for(sms, 4);
   return ws_layout(num_seqs, num_kv_heads, max_qtiles, head_dim, target).total;
+}
+
+extern "C" int specdec_attn_launch_shape(const SpecdecAttnArgs* a, int32_t* grid, int32_t* cluster_size) {
+  if (int rc = validate_paged(a)) return rc;
+  if (!grid || !cluster_size) return fail(SPECDEC_ERR_INVALID, "grid and cluster_size must be set");
+  AttnParams p = params_from(a);
+  const int D = a->kv.head_dim;
+  const bool vf8 = a->kv.v_dtype == SPECDEC_E4M3;
+  const int sms = sm_budget(a->num_sms);
+  const int target = target_items_for(sms, 0);
+  p.max_groups = ws_layout(p.B, p.KV, p.max_qtiles, D, target).max_groups;
+  const int hint = a->cluster_size;
+  if (hint != 0 && hint != 1 && hint != 8 && hint != 16)
+    return fail(SPECDEC_ERR_INVALID, "cluster_size must be 0 (automatic), 1 (none), 8 or 16");
+  if (D == 128) {
+    if (vf8)
+      choose_clusters<128, true, false>(p, hint, sms);
+    else
+      choose_clusters<128, false, false>(p, hint, sms);
+  } else {
+    choose_clusters<64, false, false>(p, hint, sms);
+  }
+  *grid = p.cluster_size > 0 ? p.num_clusters * p.cluster_size : target / 4;
+  *cluster_size = p.cluster_size;
+  return SPECDEC_OK;
 }
 
 extern "C" int specdec_ragged_plan(const SpecdecAttnArgs* args, specdec_stream_t stream) {
@@ -1441,6 +1523,7 @@ extern "C" int specdec_attention(const void* q, const void* k, const void* v, vo
   p.scale_log2 = (1.0f / sqrtf(static_cast<float>(D))) * 1.4426950408889634f;
   const int sms = device_sm_count();
   if (int rc = fill_workspace(p, workspace, workspace_bytes, B, KV, D, sms, occupancy_for(D, false, true))) return rc;
+  p.max_ctx_hint = T;
   if (D == 128)
     choose_clusters<128, false, true>(p, 0, sms);
   else

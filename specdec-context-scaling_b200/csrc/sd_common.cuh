@@ -161,6 +161,9 @@ SD_DEV uint32_t cluster_id_x() {
 SD_DEV void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// The two halves of cluster_sync: arrive (release) early, wait (acquire) later.
+SD_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+SD_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 // Address in CTA `rank`'s shared memory of the variable at this CTA's shared address `saddr`
 // (distributed shared memory), and 16-byte / 4-byte loads from it.
 SD_DEV uint32_t dsmem_addr(uint32_t saddr, uint32_t rank) {

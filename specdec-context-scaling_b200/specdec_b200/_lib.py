@@ -15,7 +15,7 @@ LIB_NAME = "libspecdec_b200.so"
 LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
 
 PAGE_TOKENS = 16
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 F32, BF16, E4M3 = 0, 1, 2
 
@@ -69,6 +69,7 @@ class Batch(ctypes.Structure):
         ("num_seqs", _i32),
         ("num_q_heads", _i32),
         ("max_q_len", _i32),
+        ("max_ctx_len", _i32),
     ]
 
 
@@ -184,6 +185,7 @@ SIGNATURES = {
     "specdec_umma_selftest": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "specdec_gather4_selftest": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp]),
     "specdec_wait_selftest": (ctypes.c_int, [_i32, _vp, _i32, _i32, _i64, _vp, _vp, _vp]),
+    "specdec_attn_launch_shape": (ctypes.c_int, [_vp, _vp, _vp]),
     "specdec_last_error": (ctypes.c_char_p, []),
     "specdec_abi_version": (ctypes.c_int, []),
     "specdec_launch_count": (_i64, []),

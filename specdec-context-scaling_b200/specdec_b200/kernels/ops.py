@@ -208,6 +208,7 @@ class RaggedBatch:
     num_seqs: int
     max_q_len: int
     total_rows: int
+    max_ctx_len: int = 0  # host-known upper bound of ctx_len (0: unknown)
 
     @classmethod
     def from_lengths(cls, q_lens, ctx_lens, device="cuda") -> "RaggedBatch":
@@ -220,7 +221,8 @@ class RaggedBatch:
             row0.append(acc)
             acc += n
         t = torch.tensor([row0, q_lens, ctx_lens], dtype=torch.int32).to(device)
-        return cls(t[0].contiguous(), t[1].contiguous(), t[2].contiguous(), len(q_lens), max(max(q_lens), 1), acc)
+        return cls(t[0].contiguous(), t[1].contiguous(), t[2].contiguous(), len(q_lens), max(max(q_lens), 1), acc,
+                   max(ctx_lens))
 
 
 def attn_workspace(batch: RaggedBatch, num_q_heads: int, cache: PagedKVCache) -> torch.Tensor:
@@ -279,6 +281,7 @@ def attn_args(q: torch.Tensor, out: torch.Tensor, cache: PagedKVCache, layer: in
             num_seqs=batch.num_seqs,
             num_q_heads=H,
             max_q_len=batch.max_q_len,
+            max_ctx_len=batch.max_ctx_len,
         ),
         kv=_paged_kv(cache, layer),
         sm_scale=scale,
@@ -299,6 +302,16 @@ def _event_handle(ev: torch.cuda.Event) -> int:
     if ev.cuda_event == 0:
         ev.record()
     return ev.cuda_event
+
+
+def launch_shape(q, cache: PagedKVCache, batch: RaggedBatch, workspace: torch.Tensor, *,
+                 cluster_size: int = 0) -> tuple[int, int]:
+    """(grid, cluster size) of the verify kernel for this call; cluster size 0 = the persistent grid."""
+    args = attn_args(q, q, cache, 0, batch, workspace, cluster_size=cluster_size)
+    grid, cs = ctypes.c_int32(0), ctypes.c_int32(0)
+    _lib.check(_lib_handle().specdec_attn_launch_shape(ctypes.byref(args), ctypes.byref(grid), ctypes.byref(cs)),
+               "attn_launch_shape")
+    return int(grid.value), int(cs.value)
 
 
 def ragged_plan(q, cache: PagedKVCache, batch: RaggedBatch, workspace: torch.Tensor, *, status=None,

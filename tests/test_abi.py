@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_abi_version(lib):
-    assert lib.specdec_abi_version() == 2
+    assert lib.specdec_abi_version() == 3
 
 
 def test_workspace_sizes_are_host_only(lib):

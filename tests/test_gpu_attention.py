@@ -269,6 +269,27 @@ def test_small_batches_on_clusters(cluster_size, lens, q_lens, fp8, H, D):
     assert torch.equal(outs[0], outs[1])
 
 
+def test_library_cluster_choice():
+    """The library's own choice (cluster_size 0): clusters only for a small batch whose host-known
+    context bound puts every group on one cluster at one tile per CTA; the persistent grid for
+    long contexts, for an unknown bound and for large batches."""
+    ops = _ops()
+    cache, *_ = build_cache([16], 2, 128, fp8=False, seed=1)
+    q = torch.zeros(5, 12, 128, dtype=torch.bfloat16, device="cuda")
+
+    def shape(q_lens, ctx, known=True):
+        batch = ops.RaggedBatch.from_lengths(q_lens, ctx)
+        if not known:
+            batch.max_ctx_len = 0
+        return ops.launch_shape(q, cache, batch, ops.attn_workspace(batch, 12, cache))
+
+    grid, cs = shape([5], [2048])
+    assert cs in (8, 16) and grid % cs == 0
+    assert shape([5], [8192])[1] == 0
+    assert shape([5], [2048], known=False)[1] == 0
+    assert shape([1] * 64, [1024] * 64)[1] == 0
+
+
 def test_plan_built_for_another_launch_shape_is_refused():
     """A plan reused by a call that would launch another grid (clusters of 8 against clusters
     of 16, or the persistent grid) is detected on the device: the call sets
