@@ -22,6 +22,9 @@ pytestmark = pytest.mark.gpu
 # logits tolerance: bf16 GEMMs in a different order and fp32-accurate attention
 # against the eager bf16-score path
 LOGIT_RTOL = 3e-2
+# the prompt pass uses torch's fused causal attention (fp32 scores and probabilities) where the
+# reference's eager prompt pass rounds scores and probabilities to bf16
+PROMPT_LOGIT_RTOL = 4e-2
 NEAR_TIE = 0.05
 
 
@@ -41,11 +44,11 @@ def _oracle(cfg, state):
     return m.eval()
 
 
-def _close(got, want, what):
+def _close(got, want, what, rtol=LOGIT_RTOL):
     scale = max(float(want.float().abs().max()), 1e-3)
     err = float((got.float() - want.float()).abs().max())
     assert torch.isfinite(got.float()).all(), what
-    assert err <= LOGIT_RTOL * scale, f"{what}: max |err| {err:.3e} vs scale {scale:.3e}"
+    assert err <= rtol * scale, f"{what}: max |err| {err:.3e} vs scale {scale:.3e}"
 
 
 @pytest.mark.parametrize("fmt", ["fp16", "v_fp8"])
@@ -237,7 +240,7 @@ def test_paged_engine_matches_reference_golden(golden, fmt):
     cache = pm.new_cache(1, 64, v_dtype)
     with torch.inference_mode():
         lg = pm.prefill(prompt, cache, 0)
-        _close(lg[0].cpu(), want["prompt_logits"], f"{fmt} prompt logits")
+        _close(lg[0].cpu(), want["prompt_logits"], f"{fmt} prompt logits", PROMPT_LOGIT_RTOL)
         lay = StepLayout(1, 5, "cuda")
         ws = ops.attn_workspace(lay.batch, cfg.heads, cache)
         lay.set(cache.lengths)
