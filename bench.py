@@ -127,6 +127,17 @@ def measured_peak():
     return 6650.0, "fallback (6.65 TB/s)"
 
 
+def measured_bf16_peak():
+    """Burst bf16 dense GEMM TFLOP/s measured on this pool (MEASURED_PEAKS.json), else the fallback."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"])
+        except (KeyError, ValueError):
+            pass
+    return 1590.0
+
+
 def dist_setup():
     import torch
 
@@ -481,6 +492,45 @@ def cpu_specdec_baseline(prompt_len=128, max_new=8, k=4, seed=0):
                       f"prompt pass of both models ({t_prefill:.2f} s); weights built in {t_build:.1f} s"}
 
 
+def measure_lmhead(steps, warmup, rows, hidden, vocab=151936, seed=8):
+    """The fused LM-head argmax (specdec_lmhead_argmax) against the unfused path it replaces
+    (cuBLAS bf16 logits + torch.argmax), each replayed as a CUDA graph: (us fused, us unfused,
+    fused TFLOP/s).  Algorithmic work 2 * rows * hidden * vocab flops; W (vocab x hidden bf16)
+    is read once."""
+    import torch
+
+    from specdec_b200.kernels import ops
+
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = torch.randn(rows, hidden, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(vocab, hidden, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    out = torch.empty(rows, dtype=torch.int32, device="cuda")
+    ws = ops.lmhead_workspace(rows)
+
+    def graph_of(fn):
+        fn()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(gr, stream=s):
+                fn()
+        torch.cuda.current_stream().wait_stream(s)
+
+        class _G:
+            def replay(self):
+                gr.replay()
+        return _G(), gr
+
+    fused, g1 = graph_of(lambda: ops.lmhead_argmax(x, w, out=out, workspace=ws))
+    unfused, g2 = graph_of(lambda: out.copy_((x @ w.t()).argmax(-1)))
+    ms_f = time_steps(fused, steps, warmup, 1) / steps
+    ms_u = time_steps(unfused, steps, warmup, 1) / steps
+    del g1, g2
+    return ms_f * 1e3, ms_u * 1e3, 2.0 * rows * hidden * vocab / (ms_f * 1e-3) / 1e12
+
+
 def measure_e2e(steps, warmup, T=8192, q=5, layers=LAYERS, seed=0):
     """Public-API path with host buffers; returns (GB/s, ms/step, h2d bytes/step, d2h bytes/step).
 
@@ -647,6 +697,7 @@ def run_ours(args, world, rank, local):
 
     _lib.load_library()
     peak, peak_kind = measured_peak()
+    bf16_peak = measured_bf16_peak()
     T, q = 8192, 5
     cache = filled_cache(LAYERS, [T], False, seed=rank)
     step = GraphStep(cache, [q], [T], seed=rank)
@@ -708,6 +759,14 @@ def run_ours(args, world, rank, local):
                        "step; algorithmic bytes 1800 per token per layer (V 512 in, codes 256 + scales 8 out, "
                        "K 512 in + 512 out)")
         extras["append_quantize_configs2"] = app
+        lm = {}
+        for rows, hidden, label in ((256, 896, "draft_256rows_h896"), (1280, 1536, "target_1280rows_h1536")):
+            us_f, us_u, tf = measure_lmhead(max(20, min(args.steps, 100)), 5, rows, hidden)
+            lm[label] = {"us_fused": round(us_f, 2), "us_cublas_plus_argmax": round(us_u, 2), "TFLOP/s": round(tf, 1),
+                         "frac_of_measured_bf16_peak": round(tf * 1e3 / bf16_peak, 4)}
+        lm["note"] = ("specdec_lmhead_argmax (tcgen05 GEMM over the 151936-row tied embedding fused with torch.argmax's "
+                      "order; no logits written) vs x @ W^T (cuBLAS) + torch.argmax; 2 rows hidden vocab flops")
+        extras["lmhead_argmax"] = lm
     if not args.no_extras:
         e_gbs, e_ms, h2d, d2h = measure_e2e(max(5, min(args.steps, 100)), 3)
         e2e = {"value": round(e_gbs * world, 3), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),

@@ -29,6 +29,9 @@
  *   specdec_trim                 <- spec_cache.trim_cache, specdec/engine/spec_cache.py:10-28
  *   specdec_ragged_plan          <- no counterpart (the reference runs batch 1); builds the
  *                                   split-KV work list for a ragged batch on the device
+ *   specdec_lmhead_argmax        <- logits = x @ embed_tokens.weight.T (model_self.py:857)
+ *                                   followed by the executors' argmax (spec_dec.py:230-236,
+ *                                   fast_spec_dec.py:246-249), fused: no logits are written
  */
 #ifndef SPECDEC_B200_H_
 #define SPECDEC_B200_H_
@@ -275,7 +278,36 @@ typedef struct SpecdecAcceptArgs {
 } SpecdecAcceptArgs;
 
 size_t specdec_accept_workspace_bytes(int32_t num_seqs, int32_t max_rows, int32_t vocab);
+/* With logits == NULL the accept call takes g[b][j] as given (computed beforehand, e.g. by
+   specdec_lmhead_argmax into that layout) and only runs the first-mismatch scan, the next
+   token and the rollback length; it then needs no workspace. */
 int specdec_greedy_accept(const SpecdecAcceptArgs* args, specdec_stream_t stream);
+
+/*
+ * Greedy tokens of `rows` hidden-state rows through the tied LM head, without the logits:
+ *     argmax[r] = argmax_j bf16( sum_d x[r][d] w[j][d] )   (j < vocab)
+ * with fp32 accumulation on the tensor cores and torch.argmax's order on the bf16 values
+ * (NaN largest, first index on ties).  max_value[r] (optional) receives the winning bf16
+ * logit.  x: bf16 [rows][x_stride] (hidden used), w: bf16 [vocab][hidden] contiguous;
+ * hidden a multiple of 64; x, w 16-byte aligned.  The workspace
+ * (specdec_lmhead_workspace_bytes(rows), 256-byte aligned) must be zero before the first
+ * call; every call leaves it zero again.  Calls sharing a workspace must not overlap.
+ */
+typedef struct SpecdecLmHeadArgs {
+  const void* x;
+  int64_t x_stride; /* elements between rows of x */
+  const void* w;
+  int32_t rows, hidden, vocab;
+  int32_t* argmax;  /* [rows] */
+  float* max_value; /* [rows] or NULL */
+  void* workspace;
+  size_t workspace_bytes;
+  int32_t* status;
+  int32_t num_sms; /* 0: every SM */
+} SpecdecLmHeadArgs;
+
+size_t specdec_lmhead_workspace_bytes(int32_t rows);
+int specdec_lmhead_argmax(const SpecdecLmHeadArgs* args, specdec_stream_t stream);
 
 /* len_out[b] = new_len[b] when 0 < new_len[b] <= cur_len[b]; otherwise
    len_out[b] = cur_len[b] and SPECDEC_STATUS_TRIM_RANGE is raised

@@ -13,6 +13,7 @@
 // their last user, so the zero-initialised workspace stays reusable and the
 // whole step can sit in a CUDA graph.
 #include <math.h>
+#include <string.h>
 
 #include "sd_common.cuh"
 #include "sd_internal.h"
@@ -197,6 +198,36 @@ __global__ void __launch_bounds__(kArgmaxThreads) accept_kernel(const AcceptPara
   if (p.len_after) p.len_after[b] = (p.len_before ? p.len_before[b] : 0) + p.keep_offset + mm;
 }
 
+// Accept from argmaxes computed beforehand (g[b][j], e.g. by the fused LM-head argmax):
+// one thread per sequence runs the first-mismatch scan of accept_kernel's last step.
+__global__ void accept_scan_kernel(const AcceptParams p) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= p.B) return;
+  const int nrows = p.n_rows[b];
+  if (nrows < 0 || nrows > p.max_rows) {
+    raise_status(p.status, SPECDEC_STATUS_ACCEPT_RANGE);
+    return;
+  }
+  if (nrows == 0) {  // inactive sequence
+    p.m[b] = 0;
+    p.next_token[b] = -1;
+    if (p.len_after) p.len_after[b] = p.len_before ? p.len_before[b] : 0;
+    return;
+  }
+  const int32_t* gb = p.g + static_cast<int64_t>(b) * p.max_rows;
+  const int kp = p.kp[b];
+  int mm = 0;
+  if (kp < 0 || kp > p.max_cands || kp > nrows) {
+    raise_status(p.status, SPECDEC_STATUS_ACCEPT_RANGE);
+  } else {
+    const int32_t* cb = p.cands + static_cast<int64_t>(b) * p.max_cands;
+    while (mm < kp && gb[mm] == cb[mm]) ++mm;
+  }
+  p.m[b] = mm;
+  p.next_token[b] = (mm < nrows) ? gb[mm] : -1;
+  if (p.len_after) p.len_after[b] = (p.len_before ? p.len_before[b] : 0) + p.keep_offset + mm;
+}
+
 __global__ void trim_kernel(const int32_t* __restrict__ cur, const int32_t* __restrict__ req,
                             int32_t* __restrict__ out, int B, int32_t* status) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -240,7 +271,31 @@ extern "C" size_t specdec_accept_workspace_bytes(int32_t num_seqs, int32_t max_r
 
 extern "C" int specdec_greedy_accept(const SpecdecAcceptArgs* a, specdec_stream_t stream) {
   if (!a) return fail(SPECDEC_ERR_INVALID, "args is NULL");
-  if (!a->logits || !a->row0 || !a->n_rows || !a->cands || !a->kp || !a->g || !a->m || !a->next_token)
+  if (!a->logits) {
+    // the argmaxes are given in g: only the scan
+    if (!a->n_rows || !a->cands || !a->kp || !a->g || !a->m || !a->next_token)
+      return fail(SPECDEC_ERR_INVALID, "n_rows, cands, kp, g, m and next_token must be set");
+    if (a->num_seqs <= 0 || a->max_rows <= 0 || a->max_cands <= 0)
+      return fail(SPECDEC_ERR_INVALID, "num_seqs, max_rows and max_cands must be positive");
+    AcceptParams p;
+    memset(&p, 0, sizeof(p));
+    p.n_rows = a->n_rows;
+    p.cands = a->cands;
+    p.kp = a->kp;
+    p.B = a->num_seqs;
+    p.max_rows = a->max_rows;
+    p.max_cands = a->max_cands;
+    p.g = a->g;
+    p.m = a->m;
+    p.next_token = a->next_token;
+    p.len_before = a->len_before;
+    p.len_after = a->len_after;
+    p.keep_offset = a->keep_offset;
+    p.status = a->status;
+    accept_scan_kernel<<<(a->num_seqs + 127) / 128, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+    return after_launch("accept_scan_kernel");
+  }
+  if (!a->row0 || !a->n_rows || !a->cands || !a->kp || !a->g || !a->m || !a->next_token)
     return fail(SPECDEC_ERR_INVALID, "logits, row0, n_rows, cands, kp, g, m and next_token must be set");
   if (a->num_seqs <= 0 || a->max_rows <= 0 || a->max_cands <= 0 || a->vocab <= 0)
     return fail(SPECDEC_ERR_INVALID, "num_seqs, max_rows, max_cands and vocab must be positive");

@@ -95,6 +95,9 @@ SD_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitL
   }
 }
 
+// warp-uniform bounded wait; returns false when any lane gave up
+SD_DEV bool warp_wait(uint64_t* bar, uint32_t parity) { return __all_sync(0xffffffffu, mbar_wait(bar, parity)); }
+
 // ---------------------------------------------------------------- bulk TMA (plain per-CTA loads)
 // 1-D bulk copy global -> shared, completion counted on `bar` in bytes.
 // src/dst 16-byte aligned, bytes a multiple of 16.

@@ -117,7 +117,5 @@ SD_DEV float warp_rows_sum(const float (&v)[NR], int lane) {
   return a[0];
 }
 
-// warp-uniform bounded wait; returns false when any lane gave up
-SD_DEV bool warp_wait(uint64_t* bar, uint32_t parity) { return __all_sync(0xffffffffu, mbar_wait(bar, parity)); }
 
 #include "verify_kernel_body.inc"

@@ -73,6 +73,23 @@ class Batch(ctypes.Structure):
     ]
 
 
+class LmHeadArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", _vp),
+        ("x_stride", _i64),
+        ("w", _vp),
+        ("rows", _i32),
+        ("hidden", _i32),
+        ("vocab", _i32),
+        ("argmax", _vp),
+        ("max_value", _vp),
+        ("workspace", _vp),
+        ("workspace_bytes", _sz),
+        ("status", _vp),
+        ("num_sms", _i32),
+    ]
+
+
 class AttnArgs(ctypes.Structure):
     _fields_ = [
         ("q", _vp),
@@ -186,6 +203,8 @@ SIGNATURES = {
     "specdec_gather4_selftest": (ctypes.c_int, [_vp, _vp, _i64, _vp, _vp, _vp, _vp]),
     "specdec_wait_selftest": (ctypes.c_int, [_i32, _vp, _i32, _i32, _i64, _vp, _vp, _vp]),
     "specdec_attn_launch_shape": (ctypes.c_int, [_vp, _vp, _vp]),
+    "specdec_lmhead_workspace_bytes": (_sz, [_i32]),
+    "specdec_lmhead_argmax": (ctypes.c_int, [_vp, _vp]),
     "specdec_last_error": (ctypes.c_char_p, []),
     "specdec_abi_version": (ctypes.c_int, []),
     "specdec_launch_count": (_i64, []),

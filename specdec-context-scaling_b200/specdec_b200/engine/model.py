@@ -202,6 +202,11 @@ class PagedModel:
         """Tied LM head (model_self.py:857): (n, hidden) -> (n, vocab)."""
         return hidden_rows @ self.embed.t()
 
+    def greedy(self, hidden_rows: torch.Tensor, out: torch.Tensor, workspace: torch.Tensor) -> torch.Tensor:
+        """Greedy tokens (n,) int32 of the tied LM head without writing the logits
+        (specdec_lmhead_argmax: the LM-head GEMM fused with torch.argmax's order)."""
+        return ops.lmhead_argmax(hidden_rows, self.embed, out=out, workspace=workspace)
+
     # ------------------------------------------------------------------ forward passes
     def step(self, tokens: torch.Tensor, layout: StepLayout, cache: PagedKVCache, workspace: torch.Tensor,
              *, status: torch.Tensor | None = None) -> torch.Tensor:

@@ -12,6 +12,8 @@ cache.  One round:
   3. greedy accept on the device: g_j = argmax(row j), m = length of the common
      prefix of (g_0 .. g_{k-1}) and (c1 .. ck); emitted tokens c1 .. cm, g_m;
      g_m becomes the new pending token;
+The draft's proposals and the target's g_j come straight from the hidden states through
+the fused LM-head argmax (the logits are never written).
   4. rollback on the device: the target keeps pending + c1 .. cm
      (len + 1 + m), the draft the same minus ck when m == k.
 
@@ -77,6 +79,9 @@ class SpecDecEngine:
         self.rounds = 0
         self.status = torch.zeros(1, **i32)
         self.acc_ws = ops.accept_workspace(num_seqs, k + 1, target.cfg.vocab, dev)
+        self.dtok = torch.zeros(num_seqs, **i32)  # the draft's greedy tokens of one step
+        self.lm_ws_d = ops.lmhead_workspace(num_seqs, dev)
+        self.lm_ws_t = ops.lmhead_workspace(num_seqs * (k + 1), dev)
         self.graph = None
         self.idx = torch.arange(k + 1, device=dev, dtype=torch.int32)
         self.active = torch.ones(num_seqs, **i32)   # 0: the sequence has its max_new tokens
@@ -115,23 +120,23 @@ class SpecDecEngine:
         tok0 = torch.stack([first, self.pending], dim=1).reshape(-1)
         self.L0.set(self.dc.lengths, q0)
         h = draft.step(tok0, self.L0, self.dc, self.ws0, status=self.status)
-        self.cands[:, 0] = draft.logits(h[self.L0.last_rows()]).argmax(-1).int()
+        self.cands[:, 0] = draft.greedy(h[self.L0.last_rows()], self.dtok, self.lm_ws_d)
         self.dc.lengths.add_(q0)
         for i in range(1, k):
             self.L1.set(self.dc.lengths, act)
             h = draft.step(self.cands[:, i - 1], self.L1, self.dc, self.ws1, status=self.status)
-            self.cands[:, i] = draft.logits(h).argmax(-1).int()
+            self.cands[:, i] = draft.greedy(h, self.dtok, self.lm_ws_d)
             self.dc.lengths.add_(act)
-        # 2. target verify of [pending, c1 .. ck]
+        # 2. target verify of [pending, c1 .. ck]; g_j of every verify row (rows b (k+1) + j)
         vt = torch.cat([self.pending.unsqueeze(1), self.cands], dim=1).reshape(-1)
         self.LV.set(self.tc.lengths, act * (k + 1))
         h = target.step(vt, self.LV, self.tc, self.wsv, status=self.status)
-        logits = target.logits(h)
-        # 3. greedy accept (+ the target's rolled-back length len + 1 + m)
-        ops.greedy_accept(logits, row0=self.LV.q_row0, n_rows=self.LV.q_len, cands=self.cands, kp=self.kp,
+        target.greedy(h, self.g.view(-1), self.lm_ws_t)
+        # 3. greedy accept from g (+ the target's rolled-back length len + 1 + m)
+        ops.greedy_accept(None, row0=self.LV.q_row0, n_rows=self.LV.q_len, cands=self.cands, kp=self.kp,
                           max_rows=k + 1, g=self.g, m=self.m, next_token=self.next_token,
                           len_before=self.tc.lengths, len_after=self.new_tlen, keep_offset=1,
-                          workspace=self.acc_ws, status=self.status)
+                          status=self.status)
         # emitted: c1 .. cm then g_m, at out[b, n_out[b] ..]
         m = self.m.unsqueeze(1)
         vals = torch.where(self.idx[:k].unsqueeze(0) < m, self.cands, self.next_token.unsqueeze(1))

@@ -419,12 +419,60 @@ def accept_workspace(num_seqs: int, max_rows: int, vocab: int, device="cuda") ->
     return torch.zeros(max(n, 256), dtype=torch.uint8, device=device)
 
 
+def lmhead_workspace(rows: int, device="cuda") -> torch.Tensor:
+    """Zero-filled workspace of lmhead_argmax; every call leaves it zeroed, so it is reusable."""
+    n = _lib_handle().specdec_lmhead_workspace_bytes(int(rows))
+    if n == 0:
+        raise ValueError(f"lmhead_argmax supports 1 .. 65536 rows, got {rows}")
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+def lmhead_argmax(x, weight, *, out=None, max_value=None, workspace=None, status=None) -> torch.Tensor:
+    """Greedy token of every row of ``x`` (rows, hidden) bf16 through the tied LM head
+    ``weight`` (vocab, hidden) bf16: argmax over the bf16-rounded logits x @ weight^T, first
+    index on ties, NaN largest (torch.argmax), without writing the logits.  Returns (rows,)
+    int32; ``max_value`` (rows,) float32 receives the winning logit when given."""
+    if x.dim() != 2 or weight.dim() != 2 or x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise ValueError("x (rows, hidden) and weight (vocab, hidden) must be 2-D bf16")
+    if x.shape[1] != weight.shape[1] or x.stride(1) != 1 or not weight.is_contiguous():
+        raise ValueError("x rows and weight rows must share a contiguous hidden dimension")
+    rows = x.shape[0]
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int32, device=x.device)
+    if workspace is None:
+        workspace = lmhead_workspace(rows, x.device)
+    args = _lib.LmHeadArgs(
+        x=x.data_ptr(), x_stride=x.stride(0), w=weight.data_ptr(), rows=rows, hidden=x.shape[1],
+        vocab=weight.shape[0], argmax=out.data_ptr(), max_value=_ptr(max_value), workspace=workspace.data_ptr(),
+        workspace_bytes=workspace.numel(), status=_ptr(status), num_sms=0)
+    _lib.check(_lib_handle().specdec_lmhead_argmax(ctypes.byref(args), _stream()), "lmhead_argmax")
+    return out
+
+
 def greedy_accept(logits, *, row0, n_rows, cands, kp, max_rows: int, g=None, m=None, next_token=None,
                   len_before=None, len_after=None, keep_offset: int = 0, workspace=None, status=None):
     """argmax of every verify row, accepted prefix length m, next token and rolled-back lengths.
 
-    ``logits`` is (rows, vocab) bf16/f32 with rows of sequence b at ``row0[b] ..``.
+    ``logits`` is (rows, vocab) bf16/f32 with rows of sequence b at ``row0[b] ..``; or None,
+    when ``g`` already holds the rows' argmaxes (lmhead_argmax) and only the accept scan runs.
     Returns (g [B, max_rows], m [B], next_token [B]) int32 device tensors."""
+    if logits is None:
+        if g is None:
+            raise ValueError("without logits, g must hold the argmaxes")
+        B = int(kp.numel())
+        dev = g.device
+        if m is None:
+            m = torch.empty(B, dtype=torch.int32, device=dev)
+        if next_token is None:
+            next_token = torch.empty(B, dtype=torch.int32, device=dev)
+        args = _lib.AcceptArgs(
+            logits=None, logits_dtype=_lib.BF16, row_stride=0, vocab=0, row0=_ptr(row0), n_rows=n_rows.data_ptr(),
+            cands=cands.data_ptr(), kp=kp.data_ptr(), num_seqs=B, max_rows=int(max_rows),
+            max_cands=int(cands.shape[1]), g=g.data_ptr(), m=m.data_ptr(), next_token=next_token.data_ptr(),
+            len_before=_ptr(len_before), len_after=_ptr(len_after), keep_offset=int(keep_offset), workspace=None,
+            workspace_bytes=0, status=_ptr(status))
+        _lib.check(_lib_handle().specdec_greedy_accept(ctypes.byref(args), _stream()), "greedy_accept")
+        return g, m, next_token
     if logits.dim() != 2 or logits.stride(1) != 1:
         raise ValueError("logits must be (rows, vocab) with contiguous vocab")
     code = _dtype_code(logits)
