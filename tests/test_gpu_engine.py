@@ -245,7 +245,11 @@ def test_paged_engine_matches_reference_golden(golden, fmt):
         ws = ops.attn_workspace(lay.batch, cfg.heads, cache)
         lay.set(cache.lengths)
         h = pm.step(g["block"].to(torch.int32).cuda().reshape(-1), lay, cache, ws)
-        _close(pm.logits(h).cpu(), want["verify_logits"], f"{fmt} verify-block logits")
+        # V-only FP8: the verify block attends over the prompt's E4M3 codes, and prompt hidden
+        # states that differ from the reference's at bf16 rounding level (fused prompt attention)
+        # flip single codes by an eighth of a step: the prompt-pass bar applies
+        _close(pm.logits(h).cpu(), want["verify_logits"], f"{fmt} verify-block logits",
+               PROMPT_LOGIT_RTOL if fmt == "v_fp8" else LOGIT_RTOL)
     N = len(want["greedy"])
     eng = SpecDecEngine(pm, PagedModel(cfg, state), 1, P, N, k=4, target_v=v_dtype, draft_v=v_dtype)
     eng.capture()
