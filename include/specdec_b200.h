@@ -325,6 +325,17 @@ int specdec_attention(const void* q, const void* k, const void* v, void* out, in
                       int32_t B, int32_t H, int32_t KV, int32_t S, int32_t T, int32_t D,
                       void* workspace, size_t workspace_bytes, specdec_stream_t stream);
 
+/* The contiguous op over a V-only FP8 dict cache (the engine's "v_fp8" format): bf16 q
+   (B,H,S,128) and k (B,KV,T,128), E4M3 V codes (B,KV,T,128) with their per-token scales
+   (B,KV,T) f32 -- the cache's "v" and "v_scale" tensors as they are.  The codes are widened
+   inside the PV product with the scale folded into the probabilities, so no dequantised
+   history is ever formed.  Replaces dequantize_kv_fp8 of the whole history followed by the
+   attention of the patched forward (specdec/kernels/patch.py:94-103, model_self.py:723-725).
+   Workspace as specdec_attention_workspace_bytes. */
+int specdec_attention_fp8v(const void* q, const void* k, const void* v_codes, const float* v_scale, void* out,
+                           int32_t B, int32_t H, int32_t KV, int32_t S, int32_t T, int32_t D, void* workspace,
+                           size_t workspace_bytes, specdec_stream_t stream);
+
 /* RMSNorm over the last dim (fp32 mean of squares; the normalised value is
    rounded to the input dtype before the weight multiply, as model_self.RMSNORM). */
 int specdec_rmsnorm(const void* x, const void* weight, void* out, int32_t dtype, int64_t rows,

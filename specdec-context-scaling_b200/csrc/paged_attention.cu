@@ -1474,9 +1474,11 @@ extern "C" size_t specdec_attention_workspace_bytes(int32_t B, int32_t H, int32_
   return specdec_attn_workspace_bytes(B, H, KV, D, S, num_sms);
 }
 
-extern "C" int specdec_attention(const void* q, const void* k, const void* v, void* out, int32_t dtype, int32_t B,
-                                 int32_t H, int32_t KV, int32_t S, int32_t T, int32_t D, void* workspace,
-                                 size_t workspace_bytes, specdec_stream_t stream) {
+// The contiguous op: bf16 / f32 K and V (v_scale NULL), or bf16 K with E4M3 V codes and
+// their per-token scales (v_scale set; the codes are widened inside the PV product).
+static int contiguous_attention(const void* q, const void* k, const void* v, const float* v_scale, void* out,
+                                int32_t dtype, int32_t B, int32_t H, int32_t KV, int32_t S, int32_t T, int32_t D,
+                                void* workspace, size_t workspace_bytes, specdec_stream_t stream) {
   // argument checks of attention_cuda (attention.cu:245-260)
   if (!q || !k || !v || !out) return fail(SPECDEC_ERR_INVALID, "tensors must be CUDA");
   if (B <= 0 || H <= 0 || KV <= 0) return fail(SPECDEC_ERR_INVALID, "batch mismatch");
@@ -1521,20 +1523,54 @@ extern "C" int specdec_attention(const void* q, const void* k, const void* v, vo
   p.num_pages = 1;
   p.max_pages = (T + kPage - 1) / kPage;
   p.scale_log2 = (1.0f / sqrtf(static_cast<float>(D))) * 1.4426950408889634f;
+  p.v_scale = v_scale;
+  if (v_scale && (reinterpret_cast<uintptr_t>(v_scale) & 3u)) return fail(SPECDEC_ERR_INVALID, "v_scale must be 4-byte aligned");
   const int sms = device_sm_count();
   if (int rc = fill_workspace(p, workspace, workspace_bytes, B, KV, D, sms, occupancy_for(D, false, true))) return rc;
   p.max_ctx_hint = T;
-  if (D == 128)
+  if (v_scale)
+    choose_clusters<128, true, true>(p, 0, sms);
+  else if (D == 128)
     choose_clusters<128, false, true>(p, 0, sms);
   else
     choose_clusters<64, false, true>(p, 0, sms);
   CUtensorMap kmap, vmap;
   if (int rc = encode_kv_map(&kmap, k, B * KV, T, D)) return rc;
-  if (int rc = encode_kv_map(&vmap, v, B * KV, T, D)) return rc;
+  if (v_scale != nullptr) {
+    // E4M3 codes (B*KV, T, 128) bytes: one 16-token page of codes = one {128, 16, 1} box
+    auto fn = get_encode_fn();
+    if (!fn) return fail(SPECDEC_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(T), static_cast<cuuint64_t>(B * KV)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(T) * D};
+    cuuint32_t box[3] = {static_cast<cuuint32_t>(D), static_cast<cuuint32_t>(kPage), 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = fn(&vmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(v), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SPECDEC_ERR_INVALID, "cuTensorMapEncodeTiled (codes) failed (%d)", static_cast<int>(r));
+  } else if (int rc = encode_kv_map(&vmap, v, B * KV, T, D)) {
+    return rc;
+  }
   CUtensorMap smap;
   memset(&smap, 0, sizeof(smap));
+  if (v_scale != nullptr) return run_attention<128, true, true>(p, kmap, vmap, smap, true, st);
   if (D == 128) return run_attention<128, false, true>(p, kmap, vmap, smap, true, st);
   return run_attention<64, false, true>(p, kmap, vmap, smap, true, st);
+}
+
+extern "C" int specdec_attention(const void* q, const void* k, const void* v, void* out, int32_t dtype, int32_t B,
+                                 int32_t H, int32_t KV, int32_t S, int32_t T, int32_t D, void* workspace,
+                                 size_t workspace_bytes, specdec_stream_t stream) {
+  return contiguous_attention(q, k, v, nullptr, out, dtype, B, H, KV, S, T, D, workspace, workspace_bytes, stream);
+}
+
+extern "C" int specdec_attention_fp8v(const void* q, const void* k, const void* v_codes, const float* v_scale,
+                                      void* out, int32_t B, int32_t H, int32_t KV, int32_t S, int32_t T, int32_t D,
+                                      void* workspace, size_t workspace_bytes, specdec_stream_t stream) {
+  if (!v_scale) return fail(SPECDEC_ERR_INVALID, "v_scale must be set");
+  if (D != 128) return fail(SPECDEC_ERR_UNSUPPORTED, "E4M3 V needs head_dim 128 (one scale group per head)");
+  return contiguous_attention(q, k, v_codes, v_scale, out, SPECDEC_BF16, B, H, KV, S, T, D, workspace,
+                              workspace_bytes, stream);
 }
 
 // ---------------------------------------------------------------- gather4 self-check

@@ -204,6 +204,8 @@ SIGNATURES = {
     "specdec_wait_selftest": (ctypes.c_int, [_i32, _vp, _i32, _i32, _i64, _vp, _vp, _vp]),
     "specdec_attn_launch_shape": (ctypes.c_int, [_vp, _vp, _vp]),
     "specdec_lmhead_workspace_bytes": (_sz, [_i32]),
+    "specdec_attention_fp8v": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _sz,
+                                              _vp]),
     "specdec_lmhead_argmax": (ctypes.c_int, [_vp, _vp]),
     "specdec_last_error": (ctypes.c_char_p, []),
     "specdec_abi_version": (ctypes.c_int, []),

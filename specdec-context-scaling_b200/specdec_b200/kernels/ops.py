@@ -134,6 +134,33 @@ def _attention_cuda(q, k, v):
     return out
 
 
+def attention_fp8v(q, k, v_codes, v_scale):
+    """The contiguous op over a V-only FP8 dict cache: q (B,H,S,128) and k (B,KV,T,128) bf16,
+    v_codes (B,KV,T,128) float8_e4m3fn and v_scale (B,KV,T,1) float32 -- the cache's "v" and
+    "v_scale" as stored.  Equals attention(q, k, dequantize_kv_fp8(v_codes, v_scale)) without
+    forming the dequantised V: the codes are widened inside the kernel's PV product."""
+    for t in (q, k, v_codes, v_scale):
+        if not t.is_cuda:
+            raise RuntimeError("tensors must be CUDA")
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:
+        raise RuntimeError("q and k must be bfloat16")
+    if v_codes.dtype != torch.float8_e4m3fn or v_scale.dtype != torch.float32:
+        raise RuntimeError("v_codes must be float8_e4m3fn and v_scale float32")
+    q, k, v_codes, v_scale = (t.contiguous() for t in (q, k, v_codes, v_scale))
+    B, H, S, D = q.shape
+    KV, T = k.shape[1], k.shape[2]
+    if tuple(v_codes.shape) != (B, KV, T, D) or v_scale.numel() != B * KV * T or k.shape[0] != B:
+        raise RuntimeError("k, v_codes and v_scale must be (B, KV, T, D), (B, KV, T, D) and (B, KV, T, 1)")
+    lib = _lib_handle()
+    out = torch.empty_like(q)
+    ws_bytes = lib.specdec_attention_workspace_bytes(B, H, KV, S, D, 0)
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=q.device)
+    rc = lib.specdec_attention_fp8v(q.data_ptr(), k.data_ptr(), v_codes.data_ptr(), v_scale.data_ptr(), out.data_ptr(),
+                                    B, H, KV, S, T, D, ws.data_ptr(), ws.numel(), _stream())
+    _lib.check(rc, "attention_fp8v")
+    return out
+
+
 def _rmsnorm_cuda(x, weight, eps):
     if not (x.is_cuda and weight.is_cuda):
         raise RuntimeError("x must be CUDA")

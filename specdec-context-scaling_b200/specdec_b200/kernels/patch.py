@@ -108,7 +108,8 @@ def _history(m, cache, key: str, cur16, dtype):
 
 def _attn_forward(self, x, cos, sin, cache=None):
     """SelfAttention.forward (model_self.py:668-800) with the eager score tensor replaced
-    by ops.attention; cache formats, FP8 quantisation and phase accounting unchanged."""
+    by ops.attention (ops.attention_fp8v over a V-only FP8 history, which is then never
+    dequantised); cache formats, FP8 quantisation and phase accounting unchanged."""
     import torch
 
     from . import ops
@@ -136,12 +137,25 @@ def _attn_forward(self, x, cos, sin, cache=None):
     else:
         v_cur = v
 
+    # V-only FP8 history (bf16 K, E4M3 V of one group per head): the kernel reads the codes
+    # and scales as the cache stores them -- the new tokens' codes are appended first, as the
+    # cache update below would -- and widens them inside its PV product, so the history is
+    # never dequantised (the reference dequantises all of it every call, patch.py:94-103)
+    fused_v = (cache is not None and fmt != "fp16" and v_on and not k_on and "v_scale" in cache
+               and "k_scale" not in cache and self.head_dim == 128 and q.dtype == torch.bfloat16
+               and codes["v"][1].shape[-1] == 1)
+    v_codes_all = v_scale_all = None
     if cache is None:
         k_all, v_all = k_cur, v_cur
     elif fmt == "fp16":
         k_all = torch.cat([cache["k"], k], dim=2)
         v_all = torch.cat([cache["v"], v], dim=2)
         cache["k"], cache["v"] = k_all, v_all
+    elif fused_v:
+        k_all = _history(m, cache, "k", k_cur, x.dtype)
+        v_codes_all = torch.cat([cache["v"], codes["v"][0]], dim=2)
+        v_scale_all = torch.cat([cache["v_scale"], codes["v"][1]], dim=2)
+        v_all = None
     else:
         k_all = _history(m, cache, "k", k_cur, x.dtype)
         v_all = _history(m, cache, "v", v_cur, x.dtype)
@@ -153,7 +167,11 @@ def _attn_forward(self, x, cos, sin, cache=None):
         path, reason = decide(m._ATTENTION_PHASE, s)
         m._record_attention_call(path, m._ATTENTION_PHASE, s, T, reason, self.heads, self.kv_heads, self.head_dim)
     if path == "fused":
+        if v_all is None:
+            v_all = m.dequantize_kv_fp8(v_codes_all, v_scale_all, x.dtype)
         out = m._fused_prefill_attention(q, k_all, v_all, self.head_dim)
+    elif v_all is None:
+        out = ops.attention_fp8v(q, k_all, v_codes_all, v_scale_all)
     else:
         out = ops.attention(q, k_all, v_all, backend="cuda")
     out = out.transpose(1, 2).contiguous().view(b, s, self.heads * self.head_dim)
@@ -171,7 +189,9 @@ def _attn_forward(self, x, cos, sin, cache=None):
     else:
         if fmt in ("fp8", "v_fp8"):
             for key in ("k", "v"):
-                if key in codes:
+                if key == "v" and v_codes_all is not None:
+                    cache["v"], cache["v_scale"] = v_codes_all, v_scale_all  # appended above
+                elif key in codes:
                     cache[key] = torch.cat([cache[key], codes[key][0]], dim=2)
                     cache[key + "_scale"] = torch.cat([cache[key + "_scale"], codes[key][1]], dim=2)
         new_cache = cache

@@ -35,6 +35,27 @@ def test_contiguous_attention_matches_golden(golden):
         assert_close_attention(got, case["fp32"], f"{name} vs fp32")
 
 
+@pytest.mark.parametrize("B,S,T", [(1, 1, 1), (1, 5, 5), (2, 5, 77), (1, 1, 300), (1, 5, 2048), (1, 5, 8192),
+                                   (2, 2, 4093)])
+def test_contiguous_attention_fp8v(B, S, T):
+    """The contiguous op over a V-only FP8 dict cache's codes and scales (the patched forward's
+    path) against the fp32 formula on the dequantised V (reference.attention_fp32 after
+    dequantize_kv_fp8), including lengths that are not multiples of the 16-token page."""
+    from oracle import engine as oeng
+    from oracle import fp8 as ofp8
+
+    ops = _ops()
+    H, KV, D = 12, 2, 128
+    g = torch.Generator().manual_seed(B * 100 + S + T)
+    q = torch.randn(B, H, S, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, KV, T, D, generator=g).to(torch.bfloat16)
+    v = torch.from_numpy(ofp8.outlier_v((B, KV, T, D), T + S)).to(torch.bfloat16)
+    codes, scale = oeng.quantize_kv_fp8(v, 128)
+    got = ops.attention_fp8v(q.cuda(), k.cuda(), codes.cuda(), scale.cuda()).cpu()
+    vd = oeng.dequantize_kv_fp8(codes, scale, torch.bfloat16)
+    assert_close_attention(got, oatt.attention_fp32(q, k, vd), f"fp8v B={B} S={S} T={T}")
+
+
 @pytest.mark.parametrize("S,T", [(1, 1), (1, 15), (1, 16), (1, 17), (5, 5), (5, 21), (2, 300), (5, 2048), (64, 64)])
 @pytest.mark.parametrize("H,KV,D", [(12, 2, 128), (14, 2, 64)])
 def test_contiguous_attention_shapes(S, T, H, KV, D):

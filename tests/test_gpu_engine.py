@@ -76,18 +76,33 @@ def test_patch_packs_match_torch_path(fmt, pack):
 
     want, cache_t = run()
     patch.set_target(oeng)
+    # every dequantisation the patched forward asks for, by token count
+    seen = []
+    orig_deq = oeng.dequantize_kv_fp8
+
+    def counting(qv, scale, dtype=torch.float16):
+        seen.append(int(qv.shape[2]))
+        return orig_deq(qv, scale, dtype)
+
+    oeng.dequantize_kv_fp8 = counting
     try:
         patch.install(pack)
         got, cache_p = run()
     finally:
         patch.restore()
         patch.set_target(None)
+        oeng.dequantize_kv_fp8 = orig_deq
     _close(got, want, f"{pack}/{fmt} logits")
     if fmt == "v_fp8":
-        # the FP8 cache state stays the engine's own quantisation
+        # the FP8 cache state stays the engine's own quantisation, bit for bit
         for lt, lp in zip(cache_t, cache_p):
             assert lt["fmt"] == lp["fmt"] == "v_fp8"
             assert lt["v"].shape == lp["v"].shape
+            assert torch.equal(lt["v"].view(torch.uint8), lp["v"].view(torch.uint8))
+            assert torch.equal(lt["v_scale"], lp["v_scale"])
+        # no history is dequantised: only the current block's own tokens (the 40-token
+        # prompt once per layer, then one token per decode step)
+        assert seen and max(seen) <= 40 and seen.count(40) == model.layers.__len__(), seen
 
 
 def test_paged_model_matches_oracle_logits():
