@@ -62,40 +62,46 @@ __global__ void __launch_bounds__(256) append_kernel(const AppendParams p) {
     if (lane == 0) raise_status(p.status, SPECDEC_STATUS_PAGE_OVERFLOW);
     return;
   }
+  // the new K / V row is read while the page id is looked up (two independent round trips)
+  const int64_t src = static_cast<int64_t>(p.row0[b] + i) * p.st + static_cast<int64_t>(h) * p.sh;
+  const int d0 = lane * PER;
+  uint2 k4 = make_uint2(0u, 0u), v4 = make_uint2(0u, 0u);
+  if (PER == 4) {
+    k4 = *reinterpret_cast<const uint2*>(p.k_new + src + d0);
+    v4 = *reinterpret_cast<const uint2*>(p.v_new + src + d0);
+  } else {
+    k4.x = *reinterpret_cast<const uint32_t*>(p.k_new + src + d0);
+    v4.x = *reinterpret_cast<const uint32_t*>(p.v_new + src + d0);
+  }
   const int page = p.page_table[static_cast<int64_t>(b) * p.max_pages + blk];
   if (page < 0 || page >= p.num_pages) {
     if (lane == 0) raise_status(p.status, SPECDEC_STATUS_BAD_PAGE);
     return;
   }
   const int64_t ph = static_cast<int64_t>(page) * p.KV + h;
-  const int64_t src = static_cast<int64_t>(p.row0[b] + i) * p.st + static_cast<int64_t>(h) * p.sh;
-  const int d0 = lane * PER;
 
   // ---- K: bf16 copy into the swizzled block
   {
     uint8_t* kblk = p.k_pool + ph * (D * 32);
     if (PER == 4) {
-      const uint2 kv = *reinterpret_cast<const uint2*>(p.k_new + src + d0);
-      *reinterpret_cast<uint2*>(kblk + kblock_offset(slot, d0)) = kv;
+      *reinterpret_cast<uint2*>(kblk + kblock_offset(slot, d0)) = k4;
     } else {
-      const uint32_t kv = *reinterpret_cast<const uint32_t*>(p.k_new + src + d0);
-      *reinterpret_cast<uint32_t*>(kblk + kblock_offset(slot, d0)) = kv;
+      *reinterpret_cast<uint32_t*>(kblk + kblock_offset(slot, d0)) = k4.x;
     }
   }
   // ---- V
   if (!VF8) {
     uint8_t* vblk = p.v_pool + ph * (D * 32);
     if (PER == 4) {
-      const uint2 vv = *reinterpret_cast<const uint2*>(p.v_new + src + d0);
-      *reinterpret_cast<uint2*>(vblk + kblock_offset(slot, d0)) = vv;
+      *reinterpret_cast<uint2*>(vblk + kblock_offset(slot, d0)) = v4;
     } else {
-      const uint32_t vv = *reinterpret_cast<const uint32_t*>(p.v_new + src + d0);
-      *reinterpret_cast<uint32_t*>(vblk + kblock_offset(slot, d0)) = vv;
+      *reinterpret_cast<uint32_t*>(vblk + kblock_offset(slot, d0)) = v4.x;
     }
   } else {
     float x[PER];
+    const __nv_bfloat16* vh = reinterpret_cast<const __nv_bfloat16*>(&v4);
 #pragma unroll
-    for (int e = 0; e < PER; ++e) x[e] = __bfloat162float(p.v_new[src + d0 + e]);
+    for (int e = 0; e < PER; ++e) x[e] = __bfloat162float(vh[e]);
     float m = 0.f;
 #pragma unroll
     for (int e = 0; e < PER; ++e) m = amax_nan(m, fabsf(x[e]));
