@@ -43,11 +43,14 @@ struct WorkItem {             // 48 bytes
   int32_t cta;                // the persistent CTA that processes the item
 };
 static_assert(sizeof(WorkItem) == 48, "work item is 48 bytes");
-// What a persistent CTA needs before its first copies: its item range, its first work
-// item and that item's first 32 page ids (0 past the item), and for after its items the
-// merge counts -- one 256-byte line.
+// What a persistent CTA needs before its first copies: its item range, its first
+// kDescItems work items (every role reads them from shared memory, so switching items
+// waits for no global load; later ones come from the item list), the first item's first 32
+// page ids (0 past the item), and for after its items the merge counts -- one 384-byte line.
+constexpr int kDescItems = 4;
 struct CtaDesc {
-  WorkItem first;  // cluster mode: the CTA's group (its item, or the group's fields when it has no pages)
+  WorkItem items[kDescItems];  // cluster mode: items[0] is the CTA's group (its item, or the
+                               // group's fields when it has no pages)
   int32_t item_begin, item_end;  // the CTA's items: [item_begin, item_end) (every CTA of the grid)
   int32_t cl_first, cl_count;    // cluster mode: the group's first cluster and cluster count (0: idle)
   int32_t pages[32];
@@ -56,10 +59,10 @@ struct CtaDesc {
   // the launch shape the plan was built for: the verify kernel runs nothing when the
   // descriptor does not match its own grid (a plan reused with another cluster choice)
   int32_t plan_magic, plan_cluster, plan_grid;
-  int32_t pad1[10];
+  int32_t pad1[6];
 };
 constexpr int32_t kPlanMagic = 0x53504c4e;
-static_assert(sizeof(CtaDesc) == 256, "CTA descriptor is 256 bytes");
+static_assert(sizeof(CtaDesc) == 384, "CTA descriptor is 384 bytes");
 struct GroupInfo {
   int32_t first_item, nsplit, b, h, q0, nq, pad0, pad1;
 };
@@ -275,7 +278,7 @@ SD_DEV void cluster_plan(const AttnParams& p) {
       d.cl_count = s_c[g];
     }
     p.items[x] = it;
-    d.first = it;
+    d.items[0] = it;
     d.item_begin = x;
     d.item_end = x + (it.page_end > it.page_begin ? 1 : 0);
     d.num_merge_wide = 0;
@@ -288,7 +291,7 @@ SD_DEV void cluster_plan(const AttnParams& p) {
   __syncthreads();
   for (int u = t; u < grid * 32; u += blockDim.x) {
     const int x = u >> 5, kk = u & 31;
-    const WorkItem& it = p.cdesc[x].first;
+    const WorkItem& it = p.cdesc[x].items[0];
     p.cdesc[x].pages[kk] = (p.page_table != nullptr && kk < it.page_end - it.page_begin)
                                ? p.page_table[static_cast<int64_t>(it.b) * p.max_pages + it.page_begin + kk]
                                : 0;
@@ -494,7 +497,8 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
     if (recorded ? s_cfirst[c] < 0 : p.cta_first[c] >= p.cta_first[c + 1]) continue;
     const WorkItem it = recorded ? s_fitem[c] : p.items[p.cta_first[c]];
     CtaDesc& d = p.cdesc[idle + c];
-    if (k == 0) d.first = it;
+    if (k == 0) d.items[0] = it;
+    if (k > 0 && k < kDescItems && p.cta_first[c] + k < p.cta_first[c + 1]) d.items[k] = p.items[p.cta_first[c] + k];
     d.pages[k] = (p.page_table != nullptr && k < it.page_end - it.page_begin)
                      ? p.page_table[static_cast<int64_t>(it.b) * p.max_pages + it.page_begin + k]
                      : 0;
@@ -714,7 +718,7 @@ SD_DEV void cluster_merge(const AttnParams& p, const CtaDesc& cd, const float* c
   static_assert(NWARP * SPW * kClusterMaxUnits >= 32, "units of a CTA in one step");
   const int quad = lane % NQ, slot = lane / NQ;
   const int CS = static_cast<int>(cluster_nctarank()), cr = static_cast<int>(cluster_ctarank());
-  const WorkItem& g = cd.first;
+  const WorkItem& g = cd.items[0];
   const int R = p.n_rep * g.nq;
   const int own = R > cr ? (R - cr + CS - 1) / CS : 0;  // rows cr, cr + CS, ...
   const int units = own * CS;
