@@ -80,6 +80,9 @@ static_assert(sizeof(PlanHeader) == 256, "plan header is 256 bytes");
 constexpr int kMaxRows = 64;  // query rows (n_rep x query positions) per work item
 constexpr int kPlanTilePages = 8;  // pages per 128-key tile of the verify kernel
 constexpr int kWholeTileMax = 4;   // the plan gives CTAs whole tiles up to this many per CTA
+// what starting one more item costs a CTA of a bandwidth-bound call, in pages (measured: about
+// 3 us per extra item against 0.18 us per page of a ragged batch, bf16 or E4M3 V)
+constexpr int kItemCostPages = 16;
 // per split item and row, one 32-byte sector: the row max (log2 units), the four
 // key-quarter partial sums and three unused words
 constexpr int kStatStride = 8;
@@ -316,7 +319,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
   }
   __shared__ int s_warp[32];
   __shared__ long long s_total;
-  __shared__ int s_rows;
+  __shared__ int s_rows, s_live;
   __shared__ int s_first[1024], s_pages[1024], s_nq[1024], s_c0[1024];
   __shared__ long long s_start[1024];
   // each persistent CTA's first item (index and copy), recorded as the items are written
@@ -327,26 +330,33 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
   if (threadIdx.x == 0) {
     s_total = 0;
     s_rows = 0;
+    s_live = 0;
   }
   for (int c = threadIdx.x; c <= kPlanCtas; c += blockDim.x) s_cfirst[c] = -1;  // -1: no item
   __syncthreads();
   long long local = 0;
   int lrows = 0;  // query rows of the groups with pages
+  int llive = 0;  // groups with pages
   for (int gi = threadIdx.x; gi < ngroups; gi += blockDim.x) {
     int b, h, q0, nq;
     const int pg = group_pages(p, gi, b, h, q0, nq);
     local += pg;
-    if (pg > 0) lrows += p.n_rep * nq;
+    if (pg > 0) {
+      lrows += p.n_rep * nq;
+      ++llive;
+    }
   }
   // warp reduce then one atomic per warp
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     local += __shfl_xor_sync(0xffffffffu, local, o);
     lrows += __shfl_xor_sync(0xffffffffu, lrows, o);
+    llive += __shfl_xor_sync(0xffffffffu, llive, o);
   }
   if ((threadIdx.x & 31) == 0) {
     atomicAdd(reinterpret_cast<unsigned long long*>(&s_total), static_cast<unsigned long long>(local));
     atomicAdd(&s_rows, lrows);
+    atomicAdd(&s_live, llive);
   }
   __syncthreads();
   const long long P = s_total;
@@ -363,6 +373,11 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
   // across many CTAs (a CTA each) still runs in one round.
   const int grid = p.target_items / 4;
   int C = static_cast<int>(min(static_cast<long long>(grid), max(P, 1LL)));
+  // Bandwidth-bound calls: every item a CTA starts costs about as much as kItemCostPages
+  // pages (its last PV and epilogue are not overlapped with the next item's tiles), so the
+  // split runs over a cost axis on which each group is preceded by that many units without
+  // pages; CTAs then finish together whatever their item counts.
+  long long ov = kItemCostPages;
   {
     const long long tile_slots = static_cast<long long>(kPlanTilePages) * grid;
     const long long k = (P + tile_slots - 1) / tile_slots;  // tiles per CTA with the whole grid
@@ -371,10 +386,14 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
       long long want = (P + per - 1) / per;
       if (s_rows <= grid) want = max(want, static_cast<long long>(s_rows));
       C = static_cast<int>(min(static_cast<long long>(C), want));
+      ov = 0;  // whole tiles: no cost axis
     }
   }
-  auto cta_of = [&](long long pos) { return static_cast<int>(((pos + 1) * C + P - 1) / P) - 1; };
-  auto range_lo = [&](int c) { return static_cast<long long>(c) * P / C; };
+  // the cost axis: pages plus ov per group with pages (every range of a bandwidth-bound call
+  // spans more than kWholeTileMax tiles > ov units, so each one holds real pages)
+  const long long Pc = P + ov * s_live;
+  auto cta_of = [&](long long pos) { return static_cast<int>(((pos + 1) * C + Pc - 1) / Pc) - 1; };
+  auto range_lo = [&](int c) { return static_cast<long long>(c) * Pc / C; };
 
   int carry = 0, wcarry = 0, ncarry = 0;
   long long pcarry = 0;
@@ -382,8 +401,10 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
     const int gi = base + threadIdx.x;
     int b = 0, h = 0, q0 = 0, nq = 0, pages = 0;
     if (gi < ngroups) pages = group_pages(p, gi, b, h, q0, nq);
+    const int cost = pages > 0 ? pages + static_cast<int>(ov) : 0;
     int chunk_pages;
-    const long long start = pcarry + block_exclusive_scan(pages, chunk_pages, s_warp);
+    // the group's pages start after its ov units on the cost axis
+    const long long start = pcarry + block_exclusive_scan(cost, chunk_pages, s_warp) + ov;
     int n = 0, c0 = 0;
     if (pages > 0) {
       c0 = cta_of(start);
@@ -443,8 +464,8 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
       it.row0 = seq_row0(p, b2);
       it.cta = c;
       p.items[carry + i] = it;
-      // range c starts inside this group: this is CTA c's first item
-      if (range_lo(c) >= gs && c < kPlanCtas) {
+      // range c starts inside this group (its cost units included): CTA c's first item
+      if (range_lo(c) >= gs - ov && c < kPlanCtas) {
         s_cfirst[c] = carry + i;
         s_fitem[c] = it;
       }
