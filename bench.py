@@ -837,9 +837,25 @@ def run_profile_case(args):
     from specdec_b200 import _lib
 
     _lib.load_library()
+    if args.profile_case == "lmhead":
+        # the target's LM-head argmax of 256 sequences' verify rows (1280 x 1536 x 151936)
+        from specdec_b200.kernels import ops
+
+        g = torch.Generator(device="cuda").manual_seed(8)
+        x = torch.randn(1280, 1536, generator=g, device="cuda").to(torch.bfloat16)
+        w = (torch.randn(151936, 1536, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        ws = ops.lmhead_workspace(1280)
+        for _ in range(args.warmup + args.steps):
+            ops.lmhead_argmax(x, w, workspace=ws)
+        torch.cuda.synchronize()
+        print(f"profile case lmhead: {args.warmup + args.steps} calls", flush=True)
+        return
     if args.profile_case == "verify8k":
         cache = filled_cache(LAYERS, [8192], False, 0)
         step = GraphStep(cache, [5], [8192], 0)
+    elif args.profile_case == "verify2k":
+        cache = filled_cache(LAYERS, [2048], False, 0)
+        step = GraphStep(cache, [5], [2048], 0)
     elif args.profile_case == "draft64":
         cache = filled_cache(2, [8192] * 64, False, 5, d=64)
         step = GraphStep(cache, [1] * 64, [8192] * 64, 5, heads=14)
@@ -872,7 +888,8 @@ def main():
     ap.add_argument("--specdec-seqs", type=int, default=256)
     ap.add_argument("--specdec-prompt", type=int, default=8192)
     ap.add_argument("--specdec-new", type=int, default=64)
-    ap.add_argument("--profile-case", choices=["verify8k", "ragged64", "ragged64-bf16", "draft64"], default=None,
+    ap.add_argument("--profile-case", choices=["verify8k", "verify2k", "ragged64", "ragged64-bf16", "draft64", "lmhead"],
+                    default=None,
                     help="only replay this workload's step graph warmup + steps times (for profilers)")
     args = ap.parse_args()
     if args.profile_case:
