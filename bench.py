@@ -49,8 +49,8 @@ H, KV, D = 12, 2, 128
 LAYERS = 28
 PAGE = 16
 # DRAM bytes (read + write) of one verify-kernel launch of the headline workload, from an
-# `ncu --set full` capture of `bench.py --profile-case verify8k` (8,649,472 read + 0 written)
-NCU_TRAFFIC_VERIFY8K = 8649472
+# `ncu --set full` capture of `bench.py --profile-case verify8k` (8,661,504 read + 0 written)
+NCU_TRAFFIC_VERIFY8K = 8661504
 
 
 def attn_bytes(T: int, q: int, fp8: bool, heads: int = H, d: int = D) -> float:
