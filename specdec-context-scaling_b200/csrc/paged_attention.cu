@@ -59,7 +59,10 @@ struct CtaDesc {
   // the launch shape the plan was built for: the verify kernel runs nothing when the
   // descriptor does not match its own grid (a plan reused with another cluster choice)
   int32_t plan_magic, plan_cluster, plan_grid;
-  int32_t pad1[6];
+  // split merge: this block's place among the merging CTAs (-1: it merges nothing), their
+  // count, and the grid-barrier arrivals per launch (0: this block does not arrive)
+  int32_t merge_cta, merge_ctas, bar_ctas;
+  int32_t pad1[3];
 };
 constexpr int32_t kPlanMagic = 0x53504c4e;
 static_assert(sizeof(CtaDesc) == 384, "CTA descriptor is 384 bytes");
@@ -70,7 +73,7 @@ struct PlanHeader {
   int32_t num_items, pages_per_split, num_groups, total_pages;
   int32_t num_merge_wide;    // split groups with >= kMergeWide splits: merge_list[0 ..)
   int32_t num_merge_narrow;  // other split groups: merge_list[max_groups - 1], [max_groups - 2], ...
-  int32_t num_ctas;          // CTAs that get pages: the last num_ctas blocks of the verify grid
+  int32_t num_ctas;          // CTAs that get pages (the verify grid's blocks: see CtaDesc)
   int32_t pad0[25];
   unsigned long long bar_arrive;  // grid-barrier arrivals of the verify kernel (own 128-byte line)
   int32_t pad1[30];
@@ -290,6 +293,9 @@ SD_DEV void cluster_plan(const AttnParams& p) {
     d.plan_magic = kPlanMagic;
     d.plan_cluster = CS;
     d.plan_grid = grid;
+    d.merge_cta = -1;
+    d.merge_ctas = 0;
+    d.bar_ctas = 0;
   }
   __syncthreads();
   for (int u = t; u < grid * 32; u += blockDim.x) {
@@ -370,8 +376,16 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
   // tiles (an 8192-token sequence: 2 x 64 CTAs of one tile, not 148 of 7 pages), so no CTA
   // pays a tile's latency for a fraction of one and the merge has fewer splits -- but no
   // fewer CTAs than split rows when the grid has that many, so the merge of rows split
-  // across many CTAs (a CTA each) still runs in one round.
+  // across many CTAs (a CTA each) still runs in one round.  Spare merge: when the grid
+  // also has a block for every query row beside the CTAs of k whole tiles, those spare
+  // blocks merge the split rows and the CTAs with pages leave at their barrier arrival --
+  // the SMs they free take the next launch's CTAs, which load their KV history while this
+  // launch merges.  (Measured: 8192-token q 1 9.3 -> 8.85 us per layer, 2048-token q 5 on
+  // the persistent grid 9.1 -> 8.65 us; taking k + 1 tiles per CTA to make room for spare
+  // blocks was slower, and so was staging several rows per spare block with bulk copies --
+  // 128 small copies per row cost ~3 us.)
   const int grid = p.target_items / 4;
+  bool spare = false;
   int C = static_cast<int>(min(static_cast<long long>(grid), max(P, 1LL)));
   // Bandwidth-bound calls: every item a CTA starts costs about as much as kItemCostPages
   // pages (its last PV and epilogue are not overlapped with the next item's tiles), so the
@@ -384,7 +398,11 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
     if (k >= 1 && k <= kWholeTileMax) {
       const long long per = k * kPlanTilePages;
       long long want = (P + per - 1) / per;
-      if (s_rows <= grid) want = max(want, static_cast<long long>(s_rows));
+      if (want > 1 && want + s_rows <= grid) {
+        spare = true;
+      } else if (s_rows <= grid) {
+        want = max(want, static_cast<long long>(s_rows));
+      }
       C = static_cast<int>(min(static_cast<long long>(C), want));
       ov = 0;  // whole tiles: no cost axis
     }
@@ -494,12 +512,20 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
     p.cta_first[c] = first;
   }
   __syncthreads();
-  // Descriptors by block: blocks 0 .. idle - 1 of the verify grid get no pages -- they are
-  // dispatched first and leave at once, so they never wait for an SM that a previous
-  // launch still holds -- and block idle + c runs CTA c's range
+  // Descriptors by block.  Merged by the CTAs with pages: blocks 0 .. idle - 1 of the verify
+  // grid get no pages -- they are dispatched first and leave at once, so they never wait for
+  // an SM that a previous launch still holds -- and block idle + c runs CTA c's range.
+  // Spare merge: block c runs CTA c's range, blocks C .. C + M - 1 merge (dispatched after
+  // the CTAs with pages, onto the SMs the previous launch's merge frees last), and the
+  // remaining blocks leave at once.  M: a block for every wide row and for the narrow rows
+  // at one warp each (a CTA has at least eight warps).
   const int idle = grid - C;
+  const int ru = p.n_rep * min(p.q_tile, p.max_q_len);
+  const int M = spare ? min(grid - C, max(wcarry * ru, (ncarry * ru + 7) / 8)) : C;
+  auto blk = [&](int c) { return spare ? c : idle + c; };
   for (int bx = threadIdx.x; bx < grid; bx += blockDim.x) {
-    const int c = bx - idle;
+    const int c = spare ? (bx < C ? bx : -1) : bx - idle;
+    const int mc = spare ? (bx >= C && bx < C + M ? bx - C : -1) : c;
     p.cdesc[bx].item_begin = c < 0 ? 0 : p.cta_first[c];
     p.cdesc[bx].item_end = c < 0 ? 0 : p.cta_first[c + 1];
     p.cdesc[bx].num_merge_wide = wcarry;
@@ -510,6 +536,9 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
     p.cdesc[bx].plan_magic = kPlanMagic;
     p.cdesc[bx].plan_cluster = 0;
     p.cdesc[bx].plan_grid = grid;
+    p.cdesc[bx].merge_cta = mc;
+    p.cdesc[bx].merge_ctas = M;
+    p.cdesc[bx].bar_ctas = (c >= 0 || mc >= 0) ? (spare ? C + M : C) : 0;
   }
   // first item and page ids: thread t fills page slot t % 32 of CTA t / 32
   for (int u = threadIdx.x; u < C * 32; u += blockDim.x) {
@@ -517,7 +546,7 @@ __global__ void __launch_bounds__(1024) plan_kernel(const AttnParams p) {
     // no work (no pages at all, P == 0): the CTA reads no descriptor
     if (recorded ? s_cfirst[c] < 0 : p.cta_first[c] >= p.cta_first[c + 1]) continue;
     const WorkItem it = recorded ? s_fitem[c] : p.items[p.cta_first[c]];
-    CtaDesc& d = p.cdesc[idle + c];
+    CtaDesc& d = p.cdesc[blk(c)];
     if (k == 0) d.items[0] = it;
     if (k > 0 && k < kDescItems && p.cta_first[c] + k < p.cta_first[c + 1]) d.items[k] = p.items[p.cta_first[c] + k];
     d.pages[k] = (p.page_table != nullptr && k < it.page_end - it.page_begin)
@@ -566,7 +595,8 @@ SD_DEV void merge_combine(MergeState& st, const MergeState& o) {
 }
 
 // s_st: NWARP x 32 states of shared memory (the caller's free staging area).
-// cta: the caller's place among the n_ctas CTAs with pages.
+// cta: the caller's place among the n_ctas merging CTAs (the CTAs with pages, or the
+// plan's spare blocks).
 // n_wide / n_narrow: the plan's merge-list counts; pre_w / pre_n: the merge-list
 // entries of this CTA's first wide unit and this warp's first narrow unit, loaded
 // before the grid barrier.
@@ -693,11 +723,13 @@ SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int cta, int war
 }
 
 // Grid-wide barrier of the persistent verify kernel: its grid is at most one CTA per
-// SM at one CTA per SM, so every CTA is resident once the kernel's CTAs run.  The
-// arrival counter grows by n_ctas (the CTAs with pages) per launch (the plan zeroes
-// it): a CTA that arrives as number `old` waits for the counter to reach the next
-// multiple of n_ctas.  Only CTAs with merge work wait.  Called by one thread per CTA;
-// bounded: false after `limit_ns` (~1 s by default).
+// SM at one CTA per SM, so every CTA is resident once the kernel's CTAs run (and no CTA
+// with pages ever waits for a spare block).  The arrival counter grows by n_ctas (the
+// plan's arrivals: the CTAs with pages, plus the merging spare blocks) per launch (the
+// plan zeroes it); every arrival of a launch follows the previous launch's completion, so
+// a CTA that arrives as number `old` waits for the counter to reach the next multiple of
+// n_ctas.  Only CTAs with merge work wait.  Called by one thread per CTA; bounded: false
+// after `limit_ns` (~1 s by default).
 SD_DEV bool grid_barrier(unsigned long long* counter, unsigned n_ctas, bool wait, uint64_t limit_ns = kWaitLimitNs) {
   __threadfence();  // this CTA's partials before its arrival
   const unsigned long long old = atomicAdd(counter, 1ull);
