@@ -318,9 +318,10 @@ def measure_config(T, q, fp8, steps, warmup, layers=LAYERS, seed=0):
     return layers * attn_bytes(T, q, fp8) * steps / (ms * 1e-3) / 1e9, ms / steps
 
 
-def measure_ragged(steps, warmup, seed=4, fp8=True):
+def measure_ragged(steps, warmup, seed=4, fp8=True, layers=LAYERS):
     """64 sequences, T ~ U[1024, 8192], q in {1, 5} 1:1, E4M3 V (or bf16 V),
-    one launch per layer over 2 layer caches."""
+    one launch per layer over `layers` layer caches (the target's 28: one plan per step serves
+    them all, as in the engine)."""
     import torch
 
     g = torch.Generator().manual_seed(seed)
@@ -328,34 +329,37 @@ def measure_ragged(steps, warmup, seed=4, fp8=True):
     q_lens = [1, 5] * 32
     perm = torch.randperm(64, generator=g).tolist()
     q_lens = [q_lens[i] for i in perm]
-    cache = filled_cache(2, lens, fp8, seed)
+    cache = filled_cache(layers, lens, fp8, seed)
     step = GraphStep(cache, q_lens, lens, seed)
     ms = time_steps(step, steps, warmup, 1)
-    byt = 2 * sum(attn_bytes(t, q, fp8) for t, q in zip(lens, q_lens))
+    byt = layers * sum(attn_bytes(t, q, fp8) for t, q in zip(lens, q_lens))
     st = int(step.status.item())
     del step, cache
     torch.cuda.empty_cache()
     if st:
         raise RuntimeError(f"device status {st:#x}")
-    return byt * steps / (ms * 1e-3) / 1e9, ms / steps, byt / 2
+    return byt * steps / (ms * 1e-3) / 1e9, ms / steps, byt / layers
 
 
-def measure_draft(steps, warmup, seed=5):
+DRAFT_LAYERS = 24  # Qwen2.5-0.5B
+
+
+def measure_draft(steps, warmup, seed=5, layers=DRAFT_LAYERS):
     """Draft-model decode attention (Qwen2.5-0.5B geometry: 14:2 heads, head_dim 64, bf16 K/V):
-    64 sequences at context 8192, q_len 1, one launch per layer over 2 layer caches."""
+    64 sequences at context 8192, q_len 1, one launch per layer over the draft's 24 layer caches."""
     import torch
 
     lens, q_lens = [8192] * 64, [1] * 64
-    cache = filled_cache(2, lens, False, seed, d=64)
+    cache = filled_cache(layers, lens, False, seed, d=64)
     step = GraphStep(cache, q_lens, lens, seed, heads=14)
     ms = time_steps(step, steps, warmup, 1)
-    byt = 2 * sum(attn_bytes(t, q, False, heads=14, d=64) for t, q in zip(lens, q_lens))
+    byt = layers * sum(attn_bytes(t, q, False, heads=14, d=64) for t, q in zip(lens, q_lens))
     st = int(step.status.item())
     del step, cache
     torch.cuda.empty_cache()
     if st:
         raise RuntimeError(f"device status {st:#x}")
-    return byt * steps / (ms * 1e-3) / 1e9, ms / steps, byt / 2
+    return byt * steps / (ms * 1e-3) / 1e9, ms / steps, byt / layers
 
 
 APPEND_BYTES_PER_TOKEN = 1800  # per layer: V bf16 512 in, codes 256 + scales 8 out, K bf16 512 in + 512 out
@@ -745,11 +749,11 @@ def run_ours(args, world, rank, local):
             gbs, mss, byt = measure_ragged(max(20, min(args.steps, 200)), 5, fp8=fp8)
             extras["ragged64_e4m3v" if fp8 else "ragged64_bf16"] = {
                 "GB/s": round(gbs, 1), "pct_of_8TBs": round(gbs / 80.0, 2), "frac_of_measured_peak": round(gbs / peak, 4),
-                "us_per_layer": round(mss / 2 * 1e3, 2), "bytes_per_layer": int(byt)}
+                "us_per_layer": round(mss / LAYERS * 1e3, 2), "bytes_per_layer": int(byt)}
         gbs, mss, byt = measure_draft(max(20, min(args.steps, 200)), 5)
         extras["draft64_d64_q1_T8192"] = {"GB/s": round(gbs, 1), "pct_of_8TBs": round(gbs / 80.0, 2),
                                           "frac_of_measured_peak": round(gbs / peak, 4),
-                                          "us_per_layer": round(mss / 2 * 1e3, 2), "bytes_per_layer": int(byt)}
+                                          "us_per_layer": round(mss / DRAFT_LAYERS * 1e3, 2), "bytes_per_layer": int(byt)}
         app = {}
         for n_tok, label in ((8192, "history_T8192"), (1, "decode_1token"), (5, "verify_5tokens")):
             gbs, us = measure_append(max(20, min(args.steps, 200)), 5, n_tok)
