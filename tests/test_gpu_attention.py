@@ -261,12 +261,16 @@ def test_draft_decode_full_size():
     ([5], [5], True, 12, 128),
     ([3000, 77, 1, 640], [5, 1, 5, 2], True, 12, 128),
     ([8192, 0, 2500], [1, 0, 1], False, 14, 64),
+    ([1024], [1], False, 12, 128),
+    ([1024, 1024], [5, 1], True, 12, 128),
 ])
 def test_small_batches_on_clusters(cluster_size, lens, q_lens, fp8, H, D):
     """Small batches with every (sequence, query tile, KV head) group on thread-block clusters
     of its own (8 or 16 CTAs: the split partials reduced in distributed shared memory, groups
     spread over several clusters joined by per-row tickets) and on the persistent grid (1),
-    against the oracle; a plan reused by the following calls of a step gives the same rows."""
+    against the oracle; a plan reused by the following calls of a step gives the same rows.
+    On the persistent grid most of these calls take the spare-block merge (blocks without
+    pages merge the split rows, wide and narrow); 3000/77/1/640 does not fit it."""
     ops = _ops()
     lens = [max(n, q) for n, q in zip(lens, q_lens)]
     lens_cache = [max(n, 1) for n in lens]
