@@ -145,11 +145,26 @@ struct AttnParams {
   int32_t cluster_size, num_clusters;
   int32_t* tickets;  // [num_clusters][kMaxRows]: arrivals of a group's clusters per row
   int32_t max_ctx_hint;  // host-known upper bound of the context lengths, 0 when unknown
+  // Paired heads (head_dim 64): KV heads 2j and 2j + 1 run as one 128-dim group j -- a page's
+  // two 2 KB head blocks are the two dim halves of one 128-dim key row, each query row
+  // carries its 64 dims in its own head's half and zeros in the other, so the 128-dim scores
+  // are the per-head ones and a query row's output is its own half of the 128-dim O row.
+  // half_heads = query heads per original KV head (n_rep / 2 here); 0 = not paired.
+  int32_t half_heads;
 };
 
 SD_DEV int seq_q_len(const AttnParams& p, int b) { return p.q_len ? p.q_len[b] : p.uni_q_len; }
 SD_DEV int seq_ctx_len(const AttnParams& p, int b) { return p.ctx_len ? p.ctx_len[b] : p.uni_ctx_len; }
 SD_DEV int seq_row0(const AttnParams& p, int b) { return p.q_row0 ? p.q_row0[b] : b * p.uni_row_stride; }
+// Output dim of O-row dim d for the query row of group head hh: d itself, or with paired
+// heads d's place in the row's own head (-1 for the other head's half).  PAIR: the kernel
+// form can run paired heads (bf16 V, 128-dim tiles, paged pools); the others compile none
+// of this.
+template <bool PAIR>
+SD_DEV int paired_dim(const AttnParams& p, int hh, int d) {
+  if (!PAIR || p.half_heads == 0) return d;
+  return (d >> 6) == hh / p.half_heads ? (d & 63) : -1;
+}
 
 // ---------------------------------------------------------------- plan
 // Key blocks a (sequence, query tile) group must read, or 0 for an empty /
@@ -600,7 +615,7 @@ SD_DEV void merge_combine(MergeState& st, const MergeState& o) {
 // n_wide / n_narrow: the plan's merge-list counts; pre_w / pre_n: the merge-list
 // entries of this CTA's first wide unit and this warp's first narrow unit, loaded
 // before the grid barrier.
-template <int D, int NWARP>
+template <int D, int NWARP, bool PAIR>
 SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int cta, int warp, int lane, int n_wide, int n_narrow,
                          int n_ctas, const GroupInfo& pre_w, const GroupInfo& pre_n) {
   constexpr int NQ = D / 4;     // dim quads
@@ -663,11 +678,12 @@ SD_DEV void merge_splits(const AttnParams& p, MergeState* s_st, int cta, int war
       o.a.w = __shfl_xor_sync(0xffffffffu, st.a.w, 16);
       merge_combine(st, o);
     }
-    if (slot == 0) {
+    const int hh = r / grp.nq, qi = grp.q0 + r % grp.nq;
+    const int dd = paired_dim<PAIR>(p, hh, quad * 4);
+    if (slot == 0 && dd >= 0) {
       const float inv = st.l > 0.f ? 1.f / st.l : 0.f;
-      const int hh = r / grp.nq, qi = grp.q0 + r % grp.nq;
       __nv_bfloat16* dst = p.out + static_cast<int64_t>(seq_row0(p, grp.b) + qi) * p.o_st +
-                           static_cast<int64_t>(grp.h * p.n_rep + hh) * p.o_sh + quad * 4;
+                           static_cast<int64_t>(grp.h * p.n_rep + hh) * p.o_sh + dd;
       uint2 pk;
       pk.x = pack_bf16(st.a.x * inv, st.a.y * inv);
       pk.y = pack_bf16(st.a.z * inv, st.a.w * inv);
@@ -762,7 +778,7 @@ SD_DEV bool grid_barrier(unsigned long long* counter, unsigned n_ctas, bool wait
 constexpr int kClusterMaxOwn = 4;   // rows per CTA: at most 32 rows over clusters of >= 8 CTAs
 constexpr int kClusterMaxUnits = 4;  // (row, peer) units per warp step: 32 units over >= 8 warps
 
-template <int D, int NWARP>
+template <int D, int NWARP, bool PAIR>
 SD_DEV void cluster_merge(const AttnParams& p, const CtaDesc& cd, const float* cl_o, const float* cl_st,
                           MergeState* s_st, int warp, int lane) {
   constexpr int NQ = D / 4;     // dim quads: lanes per row
@@ -909,8 +925,10 @@ SD_DEV void cluster_merge(const AttnParams& p, const CtaDesc& cd, const float* c
   }
   const float inv = tot.l > 0.f ? 1.f / tot.l : 0.f;
   const int hh = row / g.nq, qi = g.q0 + row % g.nq;
+  const int dd = paired_dim<PAIR>(p, hh, quad * 4);
+  if (dd < 0) return;
   __nv_bfloat16* dst = p.out + static_cast<int64_t>(g.row0 + qi) * p.o_st +
-                       static_cast<int64_t>(g.h * p.n_rep + hh) * p.o_sh + quad * 4;
+                       static_cast<int64_t>(g.h * p.n_rep + hh) * p.o_sh + dd;
   uint2 pk;
   pk.x = pack_bf16(tot.a.x * inv, tot.a.y * inv);
   pk.y = pack_bf16(tot.a.z * inv, tot.a.w * inv);
@@ -1083,16 +1101,25 @@ static int launch_k(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 bl
   return after_launch(what);
 }
 
-template <int NR, bool VF8, bool TMAP, int D, bool PP>
+template <int NR, bool VF8, bool TMAP, int D, bool PP, bool PAIR = false>
 static int launch_verify(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
                          const CUtensorMap& smap, cudaStream_t st,
                          bool pdl) {
   using Geo = V3Geom<NR < 16 ? 16 : NR, VF8, D>;
   if (p.cluster_size > 0) {
     // cluster mode: num_clusters clusters of cluster_size CTAs, one item per CTA
-    auto kern = verify_kernel<NR, VF8, TMAP, D, PP, true>;
+    auto kern = verify_kernel<NR, VF8, TMAP, D, PP, true, PAIR>;
     static bool attr[64] = {};
     set_smem_attr(kern, Geo::SMEM, attr);
+    // clusters of 16 are a non-portable size: each kernel form opts in before its first such
+    // launch (resident_clusters does so for the form it measures)
+    static bool wide[64] = {};
+    int dev = 0;
+    if (p.cluster_size > 8 && cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64 && !wide[dev]) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+        return fail(SPECDEC_ERR_CUDA, "verify_kernel: clusters of %d CTAs are not available", p.cluster_size);
+      wide[dev] = true;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.num_clusters * p.cluster_size);
     cfg.blockDim = dim3(v3_threads<VF8>());
@@ -1112,10 +1139,10 @@ static int launch_verify(const AttnParams& p, const CUtensorMap& kmap, const CUt
     return after_launch("verify_kernel");
   }
   static bool attr[64] = {};
-  set_smem_attr(verify_kernel<NR, VF8, TMAP, D, PP, false>, Geo::SMEM, attr);
+  set_smem_attr(verify_kernel<NR, VF8, TMAP, D, PP, false, PAIR>, Geo::SMEM, attr);
   // persistent: one CTA per SM, the plan's C = target_items / 4 ranges
   const int grid = p.target_items / 4;
-  return launch_k("verify_kernel", verify_kernel<NR, VF8, TMAP, D, PP, false>, dim3(grid), dim3(v3_threads<VF8>()),
+  return launch_k("verify_kernel", verify_kernel<NR, VF8, TMAP, D, PP, false, PAIR>, dim3(grid), dim3(v3_threads<VF8>()),
                   Geo::SMEM, st, pdl, p, kmap, vmap, smap);
 }
 
@@ -1193,7 +1220,7 @@ constexpr bool kTwoGroup32 = false;
 // side by side
 constexpr bool kTwoGroup32Clusters = false;
 
-template <int D, bool VF8, bool TMAP>
+template <int D, bool VF8, bool TMAP, bool PAIR = false>
 static int run_attention(AttnParams p, const CUtensorMap& kmap, const CUtensorMap& vmap, const CUtensorMap& smap,
                          bool build_plan,
                          cudaStream_t stream, void* ev_begin = nullptr, void* ev_end = nullptr) {
@@ -1206,11 +1233,11 @@ static int run_attention(AttnParams p, const CUtensorMap& kmap, const CUtensorMa
   // profiling events between the kernels need ordinary launches
   const bool pdl = ev_begin == nullptr && ev_end == nullptr;
   const int rows_max = p.n_rep * (p.q_tile < p.max_q_len ? p.q_tile : p.max_q_len);
-  const int rc = rows_max <= 8    ? launch_verify<8, VF8, TMAP, D, true>(p, kmap, vmap, smap, stream, pdl)
-                 : rows_max <= 16 ? launch_verify<16, VF8, TMAP, D, kTwoGroup16>(p, kmap, vmap, smap, stream, pdl)
+  const int rc = rows_max <= 8    ? launch_verify<8, VF8, TMAP, D, true, PAIR>(p, kmap, vmap, smap, stream, pdl)
+                 : rows_max <= 16 ? launch_verify<16, VF8, TMAP, D, kTwoGroup16, PAIR>(p, kmap, vmap, smap, stream, pdl)
                  : p.cluster_size > 0
-                     ? launch_verify<32, VF8, TMAP, D, kTwoGroup32Clusters>(p, kmap, vmap, smap, stream, pdl)
-                     : launch_verify<32, VF8, TMAP, D, kTwoGroup32>(p, kmap, vmap, smap, stream, pdl);
+                     ? launch_verify<32, VF8, TMAP, D, kTwoGroup32Clusters, PAIR>(p, kmap, vmap, smap, stream, pdl)
+                     : launch_verify<32, VF8, TMAP, D, kTwoGroup32, PAIR>(p, kmap, vmap, smap, stream, pdl);
   if (rc) return rc;
   return record_event(ev_end, stream);
 }
@@ -1317,6 +1344,13 @@ static int validate_paged(const SpecdecAttnArgs* a) {
   return SPECDEC_OK;
 }
 
+// Paired heads (AttnParams::half_heads): head_dim 64 with bf16 V and an even number of KV
+// heads whose query rows, for both heads of a pair, fit the 32-row tile: a 128-key tile then
+// streams both heads' 2 KB page blocks (64 KB of K and V per tile instead of 32 KB).
+static bool paired_geometry(int H, int KV, int D, bool vf8) {
+  return D == 64 && !vf8 && KV % 2 == 0 && 2 * (H / KV) <= 32;
+}
+
 static AttnParams params_from(const SpecdecAttnArgs* a) {
   AttnParams p;
   memset(&p, 0, sizeof(p));
@@ -1333,9 +1367,16 @@ static AttnParams params_from(const SpecdecAttnArgs* a) {
   p.H = a->batch.num_q_heads;
   p.KV = a->kv.num_kv_heads;
   p.n_rep = p.H / p.KV;
+  int D = a->kv.head_dim;
+  if (paired_geometry(p.H, p.KV, D, a->kv.v_dtype == SPECDEC_E4M3)) {
+    p.half_heads = p.n_rep;
+    p.KV /= 2;
+    p.n_rep *= 2;
+    D = 128;
+  }
   p.max_q_len = a->batch.max_q_len;
-  p.q_tile = q_tile_for(p.n_rep, a->kv.head_dim);
-  p.tile_pages = tile_pages_for(a->kv.head_dim);
+  p.q_tile = q_tile_for(p.n_rep, D);
+  p.tile_pages = tile_pages_for(D);
   p.max_qtiles = (p.max_q_len + p.q_tile - 1) / p.q_tile;
   p.k_pool = static_cast<const uint8_t*>(a->kv.k_pool);
   p.v_pool = static_cast<const uint8_t*>(a->kv.v_pool);
@@ -1352,7 +1393,7 @@ static AttnParams params_from(const SpecdecAttnArgs* a) {
 static int paged_entry(const SpecdecAttnArgs* a, cudaStream_t stream, bool plan_only) {
   if (int rc = validate_paged(a)) return rc;
   AttnParams p = params_from(a);
-  const int D = a->kv.head_dim;
+  const int D = p.half_heads > 0 ? 128 : a->kv.head_dim;  // paired heads run the 128-dim kernel
   const bool vf8 = a->kv.v_dtype == SPECDEC_E4M3;
   const int sms = sm_budget(a->num_sms);
   if (int rc = fill_workspace(p, a->workspace, a->workspace_bytes, p.B, p.KV, D, sms, occupancy_for(D, vf8, false)))
@@ -1373,10 +1414,11 @@ static int paged_entry(const SpecdecAttnArgs* a, cudaStream_t stream, bool plan_
     return after_launch("plan_kernel");
   }
   // page-row maps over the pools for the kernel's four-row gathers: K (and bf16 V) as
-  // rows of 128 bytes x 16 tokens = one dim half of a page-head block, E4M3 V as one
-  // 2048-byte row per page-head block, scales as one 64-byte row
+  // rows of 128 bytes x 16 tokens = one dim half of a page-head block (paired heads: one
+  // head's block of a page-pair block), E4M3 V as one 2048-byte row per page-head block,
+  // scales as one 64-byte row
   const int KH = D / 64;
-  const uint64_t blocks = static_cast<uint64_t>(a->kv.num_pages) * a->kv.num_kv_heads;
+  const uint64_t blocks = static_cast<uint64_t>(a->kv.num_pages) * p.KV;
   CUtensorMap kmap, vmap, smap;
   memset(&smap, 0, sizeof(smap));
   if (int rc = encode_rows_map(&kmap, a->kv.k_pool, blocks * KH, 2048)) return rc;
@@ -1390,6 +1432,7 @@ static int paged_entry(const SpecdecAttnArgs* a, cudaStream_t stream, bool plan_
   p.early_loads = (!build && a->history_ready != 0) ? 1 : 0;
   void* eb = a->split_event_begin;
   void* ee = a->split_event_end;
+  if (p.half_heads > 0) return run_attention<128, false, false, true>(p, kmap, vmap, smap, build, stream, eb, ee);
   if (D == 128) {
     return vf8 ? run_attention<128, true, false>(p, kmap, vmap, smap, build, stream, eb, ee)
                : run_attention<128, false, false>(p, kmap, vmap, smap, build, stream, eb, ee);
@@ -1405,20 +1448,25 @@ extern "C" size_t specdec_attn_workspace_bytes(int32_t num_seqs, int32_t num_q_h
                                                int32_t head_dim, int32_t max_q_len, int32_t num_sms) {
   if (num_seqs <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || max_q_len <= 0 || num_q_heads % num_kv_heads)
     return 0;
-  const int n_rep = num_q_heads / num_kv_heads;
-  const int qt = q_tile_for(n_rep, head_dim);
+  int n_rep = num_q_heads / num_kv_heads, kv = num_kv_heads, d = head_dim;
+  if (paired_geometry(num_q_heads, num_kv_heads, head_dim, false)) {  // head_dim 64 is bf16 V
+    n_rep *= 2;
+    kv /= 2;
+    d = 128;
+  }
+  const int qt = q_tile_for(n_rep, d);
   const int max_qtiles = (max_q_len + qt - 1) / qt;
   const int sms = num_sms > 0 ? num_sms : device_sm_count();
   // occupancy is not known without a device query; size for 4 CTAs per SM (an upper bound)
   const int target = target_items_for(sms, 4);
-  return ws_layout(num_seqs, num_kv_heads, max_qtiles, head_dim, target).total;
+  return ws_layout(num_seqs, kv, max_qtiles, d, target).total;
 }
 
 extern "C" int specdec_attn_launch_shape(const SpecdecAttnArgs* a, int32_t* grid, int32_t* cluster_size) {
   if (int rc = validate_paged(a)) return rc;
   if (!grid || !cluster_size) return fail(SPECDEC_ERR_INVALID, "grid and cluster_size must be set");
   AttnParams p = params_from(a);
-  const int D = a->kv.head_dim;
+  const int D = p.half_heads > 0 ? 128 : a->kv.head_dim;
   const bool vf8 = a->kv.v_dtype == SPECDEC_E4M3;
   const int sms = sm_budget(a->num_sms);
   const int target = target_items_for(sms, 0);

@@ -94,6 +94,17 @@ def test_paged_attention_draft_geometry(S):
     assert_close_attention(got, ref, f"14:2 d64 S={S}")
 
 
+@pytest.mark.parametrize("H,KV", [(28, 4), (20, 2), (8, 1), (34, 2)])
+@pytest.mark.parametrize("S", [1, 3])
+def test_paged_attention_d64_head_pairs(H, KV, S):
+    """head_dim 64 runs KV-head pairs as 128-dim groups (both heads' page blocks in one tile,
+    each query row's dims in its own head's half) when the KV heads pair up and a pair's query
+    rows fit the 32-row tile -- 28:4 (two pairs) and 20:2 -- and the 64-dim kernel otherwise
+    (8:1, 34:2); every form against the oracle."""
+    got, ref, *_ = _paged_case([900, 130, 8192], [S, S, S], H, KV, 64, False, seed=H * 10 + KV + S)
+    assert_close_attention(got, ref, f"{H}:{KV} d64 S={S}")
+
+
 def test_paged_attention_matches_eager_reference_fp8():
     got, _, q, ks, vrefs = _paged_case([2048], [5], 12, 2, 128, True, seed=99)
     ref = oracle_rows(q, ks, vrefs, [5], eager=True)
