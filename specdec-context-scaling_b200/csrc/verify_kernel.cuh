@@ -51,15 +51,17 @@ struct V3Geom {
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
   static_assert(!VF8 || D == 128, "E4M3 V needs head_dim 128");
   static constexpr int KH = D / 64;                      // 128-byte dim halves of a K row
-  static constexpr int NS = VF8 ? 2 : (D == 128 ? 3 : 6);  // ring depth (tiles)
+  // ring depth (tiles).  E4M3: the converter warps widen a tile's V codes into the K half of
+  // its own stage once QK^T of the tile has read K (no separate widened-V buffers), so four
+  // 48.5 KB stages fit; the stage is free after PV
+  static constexpr int NS = VF8 ? 4 : (D == 128 ? 3 : 6);
   static constexpr int KT = 16384 * KH;                  // K tile bytes
   static constexpr int VT = VF8 ? 16384 : 16384 * KH;    // V tile bytes as staged
   static constexpr int ST = VF8 ? 512 : 0;               // 128 scales
   static constexpr int V_OFF = D == 64 ? 0 : NS * KT;
   static constexpr int K_OFF = D == 64 ? NS * VT : 0;
   static constexpr int S_OFF = (D == 64 ? K_OFF + NS * KT : V_OFF + NS * VT);
-  static constexpr int VC_OFF = ((S_OFF + NS * ST + 1023) / 1024) * 1024;  // widened V (E4M3 only)
-  static constexpr int Q_OFF = VC_OFF + (VF8 ? 2 * 32768 : 0);
+  static constexpr int Q_OFF = ((S_OFF + NS * ST + 1023) / 1024) * 1024;
   static constexpr int QH = NR * 128;                    // one dim half of Q: [NR rows][128 B]
   static constexpr int QB = NR * 256;                    // one P buffer: [128 keys][NR rows x 2 B], MN-major
   static constexpr int P_OFF = Q_OFF + KH * QH;
