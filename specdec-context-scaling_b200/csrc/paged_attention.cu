@@ -1553,13 +1553,10 @@ static int static_scratch(void** out) {
 
 extern "C" int specdec_paged_attention_noalloc(const SpecdecAttnArgs* args, specdec_stream_t stream) {
   if (int rc = validate_paged(args)) return rc;
-  const int n_rep = args->batch.num_q_heads / args->kv.num_kv_heads;
-  const int qt = q_tile_for(n_rep, args->kv.head_dim);
-  const int max_qtiles = (args->batch.max_q_len + qt - 1) / qt;
-  const int sms = sm_budget(args->num_sms);
+  // the same size a caller workspace would need (head_dim-64 KV-head pairs included)
   const size_t need =
-      ws_layout(args->batch.num_seqs, args->kv.num_kv_heads, max_qtiles, args->kv.head_dim, target_items_for(sms, 0))
-          .total;
+      specdec_attn_workspace_bytes(args->batch.num_seqs, args->batch.num_q_heads, args->kv.num_kv_heads,
+                                   args->kv.head_dim, args->batch.max_q_len, sm_budget(args->num_sms));
   if (need > kStaticScratchBytes)
     return fail(SPECDEC_ERR_WORKSPACE,
                 "this batch needs %zu bytes of scratch; the static scratch of the no-allocation entry point "

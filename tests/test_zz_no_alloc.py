@@ -37,12 +37,12 @@ def _noalloc_call(q, cache, batch):
     return out
 
 
-def _case(lens, q_lens, fp8, seed):
+def _case(lens, q_lens, fp8, seed, H=12, D=128):
     from specdec_b200.kernels import ops
 
-    cache, ks, vrefs = build_cache(lens, 2, 128, fp8=fp8, seed=seed)
+    cache, ks, vrefs = build_cache(lens, 2, D, fp8=fp8, seed=seed)
     batch = ops.RaggedBatch.from_lengths(q_lens, lens)
-    q = torch.randn(batch.total_rows, 12, 128, generator=torch.Generator().manual_seed(seed)).to(torch.bfloat16)
+    q = torch.randn(batch.total_rows, H, D, generator=torch.Generator().manual_seed(seed)).to(torch.bfloat16)
     return cache, batch, q.cuda(), oracle_rows(q, ks, vrefs, q_lens)
 
 
@@ -52,6 +52,7 @@ def test_noalloc_matches_workspace_entry_two_calls():
     cases = [
         _case([8192], [5], fp8=True, seed=41),               # batch-1 verify, many splits
         _case([300, 2048, 77, 1500], [1, 5, 5, 1], fp8=False, seed=42),  # ragged mixed rows
+        _case([8192, 640], [1, 1], fp8=False, seed=43, H=14, D=64),     # draft decode (KV-head pairs)
     ]
     for cache, batch, q, ref in cases:
         got = _noalloc_call(q, cache, batch)
