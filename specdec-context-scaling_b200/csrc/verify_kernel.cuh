@@ -1,6 +1,6 @@
 // verify_kernel.cuh -- split-KV decode / verify attention on the fifth-generation
-// tensor cores (tcgen05, TMEM accumulators) for head_dim 128.  Included inside
-// namespace sd by paged_attention.cu, after split_kernel.cuh.
+// tensor cores (tcgen05, TMEM accumulators) for head_dim 128 and 64 (head_dim-64 KV-head
+// pairs run as 128-dim groups).  Included inside namespace sd by paged_attention.cu.
 //
 // Persistent CTAs (one per SM) over a balanced page range, 320 threads (448 for E4M3 V):
 //   warps 0-7  softmax + epilogue; warp w owns keys 32 (w % 4) .. +31 of each
@@ -11,13 +11,14 @@
 //              image of the pool; V likewise, or raw E4M3 rows + per-token scales),
 //              and the Q rows of each item
 //   warp 9     MMA issuer (one lane) and owner of the TMEM allocation
-//   warps 10-13 (E4M3 V only) converters: widen each tile's E4M3 rows to f16 in
-//              shared memory while the softmax warps work on the same tile
+//   warps 10-13 (E4M3 V only) converters: hand each tile's per-token scales to the
+//              softmax, then widen its E4M3 rows to f16 over the tile's K (once QK^T
+//              has read it) while the softmax warps work on the same tile
 // Per tile t (buffer b = t & 1):
 //   S^T[b] (128 keys x NR rows, fp32, TMEM)  = K_tile . Q^T            (8 x K=16 MMAs)
 //   softmax warps: row maxima over the tile, lazy online rescale of O (only when a
 //   row max grows by more than 2^8), P = exp2(S - M) written to shared memory as
-//   the K-major B operand; E4M3 tiles are widened to f16 in shared memory and the
+//   the MN-major B operand; E4M3 tiles are widened to f16 in shared memory and the
 //   per-token scale is folded into P
 //   O^T (128 dims x NR rows, fp32, TMEM)    += V_tile^T . P^T           (8 MMAs)
 // QK^T of tile t+1 is issued before PV of tile t, so softmax and MMAs overlap.
