@@ -20,7 +20,10 @@
 //                                balanced page range) tcgen05 QK^T / PV with TMEM
 //                                accumulators, see verify_kernel.cuh.
 //      The same kernel merges the split partials of groups with more than one
-//      split after a grid barrier (merge_splits).
+//      split after a grid barrier (merge_splits: by the CTAs with pages, or by spare
+//      blocks without pages where the grid has room), or -- small batches of short
+//      contexts -- inside thread-block clusters through distributed shared memory
+//      (cluster_merge).  head_dim-64 KV-head pairs run as 128-dim groups.
 #include <cudaTypedefs.h>
 
 #include <math.h>
